@@ -1,0 +1,367 @@
+"""Benchmark of the joint-attention forward + backward on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2] [--impl ours|reference]
+
+A step is one forward + backward of the op (axial RoPE inside) over one
+synthetic batch of the named configuration, inputs resident in HBM. With N > 1
+(launched under torch.distributed.run, one rank per GPU) every rank runs its
+own batch x head partition of the workload with no collective on the data
+path (weak scaling); the timed region is bracketed by a barrier and a device
+synchronise, and the maximum time over ranks is reported.
+
+Rank 0 prints one JSON line: the metric (TFLOP/s, FlashAttention accounting
+14*B*H*S^2*D), the roofline of the dominant kernel (the backward kernel,
+timed live with CUDA events around its own launches), the end-to-end number
+through the public API with host buffers, the CPU baseline (the oracle port
+on the host cores, a bounded sample), and the SM clocks seen while timing.
+
+`--impl reference` times the reference's arithmetic on the host cores instead:
+the reference's Candle code cannot be built here (no Rust toolchain), so the
+CPU restatement in oracle/ stands in for it, on a bounded sample per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "joint-attn fwd+bwd TFLOP/s (bf16, FlashAttention accounting 14*B*H*S^2*D)"
+UNIT = "TFLOP/s"
+
+
+def _env_int(name, default):
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"bf16": d.get("bf16_tflops"), "bf16_sustained": d.get("bf16_tflops_sustained"),
+                "hbm": d.get("hbm_gbs"), "source": "measured"}
+    return {"bf16": 1590.0, "bf16_sustained": 1400.0, "hbm": 6650.0, "source": "fallback"}
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while timing."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+        self.lines: list[str] = []
+        self._t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.dev)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except (OSError, ValueError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self._t is not None:
+            self._t.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------- CPU oracle
+def cpu_oracle_sample(cfg, budget_s: float = 12.0, min_heads: int = 1):
+    """Times the oracle port (numpy fp32) on whole heads of the workload until
+    about `budget_s` seconds of CPU work; returns (TFLOP/s, heads, seconds)."""
+    import numpy as np
+
+    from foundry_trainer_b200 import configs
+    from oracle import attn_oracle as orc
+    q, k, v, d_o = configs.make_inputs(cfg, batch=1)
+    pos = configs.positions(cfg.txt, cfg.grid).numpy()
+    qn, kn, vn, dn = (t.float().numpy() for t in (q, k, v, d_o))
+    heads, t0 = 0, time.perf_counter()
+    while heads < cfg.H and (heads < min_heads or time.perf_counter() - t0 < budget_s):
+        orc.attn_fwd_bwd_bshd(qn, kn, vn, dn, "f32", heads=[heads], rope_pos=pos)
+        heads += 1
+    dt = time.perf_counter() - t0
+    flops = 14.0 * heads * cfg.S * cfg.S * cfg.D
+    return flops / dt / 1e12, heads, dt, np.__version__
+
+
+def run_reference(args, cfg, rank):
+    """The reference arm: the oracle port on the host cores, rank 0 only."""
+    if rank != 0:
+        return
+    import numpy as np  # noqa: F401
+
+    from foundry_trainer_b200 import configs
+    from oracle import attn_oracle as orc
+    q, k, v, d_o = configs.make_inputs(cfg, batch=1)
+    pos = configs.positions(cfg.txt, cfg.grid).numpy()
+    qn, kn, vn, dn = (t.float().numpy() for t in (q, k, v, d_o))
+    head = [0]
+    for _ in range(args.warmup):
+        orc.attn_fwd_bwd_bshd(qn, kn, vn, dn, "f32", heads=head, rope_pos=pos)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        orc.attn_fwd_bwd_bshd(qn, kn, vn, dn, "f32", heads=head, rope_pos=pos)
+    dt = time.perf_counter() - t0
+    flops = 14.0 * 1 * cfg.S * cfg.S * cfg.D * args.steps
+    value = flops / dt / 1e12
+    cores = os.cpu_count()
+    sample = (f"1 of {cfg.H} heads of {cfg.name} (B=1, S={cfg.S}, D={cfg.D}) fwd+bwd per step, "
+              f"fp32 numpy restatement of lib.rs:133-263 with RoPE (Candle CPU build unavailable: "
+              f"no Rust toolchain)")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt * 1000.0 / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, configs.make_inputs)",
+        "config": {"workload": cfg.name, "B": cfg.B, "H": cfg.H, "S": cfg.S, "D": cfg.D,
+                   "txt": cfg.txt, "img_grid": cfg.grid, "rope": "axial (t,h,w,l), theta 10000"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------- ours
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="c2", choices=["c1", "c2", "c4", "c5"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    rank = _env_int("RANK", 0)
+    world = _env_int("WORLD_SIZE", 1)
+    local = _env_int("LOCAL_RANK", 0)
+
+    from foundry_trainer_b200 import configs
+    cfg = configs.CONFIGS[args.config]
+
+    if args.impl == "reference":
+        run_reference(args, cfg, rank)
+        return
+
+    import ctypes as C
+
+    import torch
+    import torch.distributed as dist
+
+    from foundry_trainer_b200 import _lib, ops
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+
+    # weak scaling: each rank owns one batch x head partition of cfg's size
+    q, k, v, d_o = (t.to(dev) for t in configs.make_inputs(cfg))
+    pos = configs.positions(cfg.txt, cfg.grid).to(dev)
+    rope = ops.Rope(pos)
+    o = torch.empty_like(q)
+    lse = torch.empty((cfg.B, cfg.H, cfg.S), device=dev, dtype=torch.float32)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    flush_buf = torch.empty(256 * 1024 * 1024 // 4, device=dev, dtype=torch.float32)
+    lib = _lib.load()
+
+    def step():
+        ops.attn_fwd(q, k, v, rope=rope, out=o, lse=lse)
+        ops.attn_bwd(q, k, v, o, d_o, lse, rope=rope, dq=dq, dk=dk, dv=dv)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if ops.device_status() != 0:
+        raise RuntimeError("device-side bounded wait expired during warm-up")
+
+    K = args.steps
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    lib.fa_timing_enable(1)
+    for kid in (0, 1):  # drop anything recorded before the timed region
+        lib.fa_timing_read(kid, C.byref(C.c_double()), C.byref(C.c_int()))
+    sampler = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    wall0 = time.perf_counter()
+    for i in range(K):
+        flush_buf.zero_()  # L2 (126 MB) flushed between timed steps, outside the events
+        starts[i].record()
+        step()
+        ends[i].record()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - wall0
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    lib.fa_timing_enable(0)
+    kt = {}
+    for kid, name in ((0, "fwd"), (1, "bwd")):
+        ms, n = C.c_double(), C.c_int()
+        _lib.check(lib.fa_timing_read(kid, C.byref(ms), C.byref(n)), "fa_timing_read")
+        kt[name] = (ms.value, n.value)
+    if ops.device_status() != 0:
+        raise RuntimeError("device-side bounded wait expired while timing")
+    step_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    t = torch.tensor([step_ms, kt["bwd"][0] / max(kt["bwd"][1], 1),
+                      kt["fwd"][0] / max(kt["fwd"][1], 1)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    step_ms_max, bwd_ms, fwd_ms = t.tolist()
+
+    flops_step = cfg.flops_fwd_bwd()
+    value = world * K * flops_step / (step_ms_max / 1e3) / 1e12
+
+    peaks = _peaks()
+    timed_seconds = step_ms_max / 1e3
+    peak_kind = "bf16_sustained" if timed_seconds > 2.0 else "bf16"
+    peak = peaks[peak_kind]
+    bwd_flops = cfg.flops_bwd()
+    achieved = bwd_flops / (bwd_ms / 1e3) / 1e12
+    traffic = None
+    tf = ROOT / "profiles" / "traffic.json"
+    if tf.exists():
+        try:
+            traffic = json.loads(tf.read_text()).get(cfg.name, {}).get("attn_bwd_kernel")
+        except (ValueError, AttributeError):
+            traffic = None
+    roofline = {"kernel": "attn_bwd_kernel", "bound": "tensor", "achieved": achieved,
+                "peak": peak, "unit": UNIT, "frac": achieved / peak, "traffic": traffic,
+                "peak_source": f"{peaks['source']} {peak_kind}",
+                "fwd_kernel": {"achieved": cfg.flops_fwd() / (fwd_ms / 1e3) / 1e12,
+                               "ms": fwd_ms},
+                "bwd_kernel_ms": bwd_ms,
+                "flops_per_launch": bwd_flops}
+
+    # ---- end to end through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        hq, hk, hv, hdo = (x.cpu().pin_memory() for x in (q, k, v, d_o))
+        ho, hdq, hdk, hdv = (torch.empty_like(x, device="cpu").pin_memory() for x in (o, dq, dk, dv))
+        h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv, hdo))
+        d2h = sum(x.numel() * x.element_size() for x in (ho, hdq, hdk, hdv))
+
+        def e2e_step():
+            q.copy_(hq, non_blocking=True)
+            k.copy_(hk, non_blocking=True)
+            v.copy_(hv, non_blocking=True)
+            d_o.copy_(hdo, non_blocking=True)
+            step()
+            ho.copy_(o, non_blocking=True)
+            hdq.copy_(dq, non_blocking=True)
+            hdk.copy_(dk, non_blocking=True)
+            hdv.copy_(dv, non_blocking=True)
+
+        for _ in range(args.warmup):
+            e2e_step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(K):
+            e2e_step()
+        s1.record()
+        torch.cuda.synchronize()
+        te = torch.tensor([s0.elapsed_time(s1)], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e = {"value": world * K * flops_step / (te.item() / 1e3) / 1e12, "unit": UNIT,
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "ms_per_step": te.item() / K,
+               "path": "ops.attn_fwd + ops.attn_bwd (C ABI fa_fwd/fa_bwd) with pinned host "
+                       "q,k,v,dO in and o,dq,dk,dv out each step"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v_cpu, heads, secs, _ = cpu_oracle_sample(cfg)
+        cpu = {"value": v_cpu, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+               "sample": f"{heads} of {cfg.H} heads of {cfg.name} fwd+bwd with RoPE, fp32 numpy "
+                         f"oracle, {secs:.1f} s"}
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    launches_per_step = 8  # rope q,k + fwd; rope q,k + delta + bwd + dQ cast
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
+        "warmup": args.warmup, "ms_per_step": step_ms_max / K, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded torch.Generator, q,k,v ~ 0.5*N(0,1), dO ~ N(0,1))",
+        "config": {"workload": f"{cfg.name}: B={cfg.B} H={cfg.H} S={cfg.S} "
+                               f"({cfg.txt} text + {cfg.grid}x{cfg.grid} image) D={cfg.D} "
+                               f"per rank, non-causal, axial RoPE inside the op",
+                   "per_rank_B": cfg.B, "H": cfg.H, "S": cfg.S, "D": cfg.D,
+                   "l2": "flushed between timed steps (256 MB write outside the step events)",
+                   "parallelism": f"batch-sharded x{world}, no collective on the data path"},
+        "roofline": roofline,
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "gpu_launches": launches_per_step * K,
+        "clocks": clocks,
+        "wall_s_timed": wall,
+    }
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

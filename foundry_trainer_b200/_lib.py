@@ -1,0 +1,123 @@
+"""ctypes binding of the C ABI in include/foundry_attn.h.
+
+The library is the product path: there is no CPU or PyTorch fallback. If
+`lib/libfoundry_attn.so` is missing, loading raises instead of degrading.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = _PKG / "lib" / "libfoundry_attn.so"
+SELFTEST_PATH = _PKG / "lib" / "libfa_selftest.so"
+
+FA_OK = 0
+FA_ERR_INVALID_ARG = 1
+FA_ERR_UNSUPPORTED = 2
+FA_ERR_ALIGNMENT = 3
+FA_ERR_LAUNCH = 4
+FA_ERR_DEVICE_TIMEOUT = 5
+FA_ERR_WORKSPACE = 6
+FA_ERR_NO_DEVICE = 7
+FA_ERR_TOO_LARGE = 8
+
+FA_DTYPE_F32 = 0
+FA_DTYPE_BF16 = 1
+
+
+class FaError(RuntimeError):
+    """A non-zero status returned by the C ABI."""
+
+    def __init__(self, status: int, where: str, message: str):
+        super().__init__(f"{where}: {message} (status {status})")
+        self.status = status
+
+
+class fa_tensor_t(C.Structure):
+    _fields_ = [("data", C.c_void_p), ("stride_b", C.c_int64), ("stride_s", C.c_int64),
+                ("stride_h", C.c_int64), ("stride_d", C.c_int64)]
+
+
+class fa_rope_t(C.Structure):
+    _fields_ = [("pos", C.c_void_p), ("n_axes", C.c_int), ("axis_dim", C.c_int),
+                ("theta", C.c_float)]
+
+
+_T = C.POINTER(fa_tensor_t)
+_R = C.POINTER(fa_rope_t)
+_F = C.c_void_p  # float* (device)
+
+# name -> (restype, argtypes)
+SIGNATURES = {
+    "fa_fwd": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _T, _T, _T, _T, _F,
+                         C.c_float, _R, C.c_void_p, C.c_size_t, C.c_void_p]),
+    "fa_fwd_workspace_bytes": (C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _R]),
+    "fa_bwd": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _T, _T, _T, _T, _T, _F,
+                         _T, _T, _T, C.c_float, _R, C.c_int, C.c_void_p, C.c_size_t, C.c_void_p]),
+    "fa_bwd_workspace_bytes": (C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _R,
+                                            C.c_int]),
+    "fa_rope_apply": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _T, _T, _R, C.c_int,
+                                C.c_void_p]),
+    "fa_fwd_partial": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _T, _T, _T,
+                                 _T, _F, C.c_float, C.c_void_p]),
+    "fa_lse_merge": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _F, _F, _T, _F,
+                               C.c_int, C.c_void_p]),
+    "fa_bwd_delta": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _T, _T, _F,
+                               C.c_void_p]),
+    "fa_bwd_partial": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _T, _T, _T,
+                                 _T, _F, _F, _F, _F, _F, C.c_float, C.c_void_p]),
+    "fa_cast_f32": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _F, _T, C.c_float, _R,
+                              C.c_void_p]),
+    "fa_timing_enable": (C.c_int, [C.c_int]),
+    "fa_timing_read": (C.c_int, [C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_int)]),
+    "fa_status_string": (C.c_char_p, [C.c_int]),
+    "fa_device_status": (C.c_int, []),
+    "fa_abi_version": (C.c_int, []),
+    "fa_build_info": (C.c_char_p, []),
+}
+
+_lib = None
+_selftest = None
+
+
+def load() -> C.CDLL:
+    """Loads libfoundry_attn.so (once). Raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise FaError(-1, "load", f"{LIB_PATH} is missing; run `python -m foundry_trainer_b200.build`")
+        lib = C.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+def load_selftest() -> C.CDLL:
+    global _selftest
+    if _selftest is None:
+        if not SELFTEST_PATH.exists():
+            raise FaError(-1, "load", f"{SELFTEST_PATH} is missing; run the build")
+        st = C.CDLL(str(SELFTEST_PATH))
+        st.fa_selftest_umma.restype = C.c_int
+        st.fa_selftest_umma.argtypes = [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                        C.c_void_p]
+        _selftest = st
+    return _selftest
+
+
+def status_string(status: int) -> str:
+    return load().fa_status_string(int(status)).decode()
+
+
+def check(status: int, where: str) -> None:
+    if status != FA_OK:
+        raise FaError(status, where, status_string(status))
+
+
+def loaded_path() -> str:
+    return os.fspath(LIB_PATH)

@@ -1,0 +1,472 @@
+// attn_bwd_sm100.cu — bf16 joint-attention backward for sm_100a.
+//
+// Gradient of O = softmax(Q K^T * scale) V, the hand-written backward of the
+// reference op (crates/foundry-spike/src/lib.rs:216-263):
+//   P   = exp(S*scale - LSE)              (recomputed from the saved LSE)
+//   dV  = P^T dO                          (lib.rs:244)
+//   dP  = dO V^T                          (lib.rs:243)
+//   dS  = P * (dP - Delta),  Delta = rowsum(dO * O)   (= rowsum(dP*P), lib.rs:246-250)
+//   dQ  = scale * dS K,  dK = scale * dS^T Q          (lib.rs:252-257)
+// The reference forms dS in fp32 and runs dQ/dK as fp32 GEMMs; here dS is
+// rounded to bf16 for the tensor core with fp32 accumulation.
+//
+// One CTA owns one 128-key K/V tile of one (b, h) and walks all 128-row Q
+// tiles (K/V stationary):
+//   warp 8      TMA producer: K, V once; Q_i, dO_i, LSE_i, Delta_i per step
+//   warp 9      tcgen05 MMA issuer, TMEM owner
+//   warps 0-3   softmax backward, one key row per thread; dV epilogue
+//   warps 4-7   dQ drain (fp32 vector reductions into dq_acc); dK epilogue
+// TMEM (512 columns):
+//   A [0,128)    S^T_i, then P^T_i (bf16, cols 0-63) | dS^T_i (bf16, 64-127)
+//   B [128,256)  dP^T_i, then dQ_i (fp32, query rows)
+//   dV [256,384) dK [384,512)   accumulators over all Q tiles
+// Every MMA that overwrites columns another MMA reads waits for that MMA's
+// commit first; dQ_i is drained while S^T_{i+1} runs.
+#include "attn_common.h"
+#include "rope.cuh"
+#include "sm100_ptx.cuh"
+
+namespace fa {
+namespace bwd {
+
+constexpr int kRows = 128;
+constexpr int kTileBytes = 32768;
+constexpr int kBlkBytes = 16384;
+constexpr int kThreads = 320;
+
+constexpr int kOffK = 0;
+constexpr int kOffV = kOffK + kTileBytes;
+constexpr int kOffQ = kOffV + kTileBytes;     // 2 stages
+constexpr int kOffDO = kOffQ + 2 * kTileBytes;  // 2 stages
+constexpr int kOffDS = kOffDO + 2 * kTileBytes;
+constexpr int kOffLse = kOffDS + kTileBytes;    // 2 x 512 B
+constexpr int kOffDelta = kOffLse + 1024;       // 2 x 512 B
+constexpr int kOffBar = kOffDelta + 1024;
+constexpr int kNumBars = 16;
+constexpr int kOffMisc = kOffBar + kNumBars * 8;
+constexpr int kSmemBytes = kOffMisc + 64;
+
+constexpr int B_KV = 0;
+constexpr int B_QFULL = 1;    // + stage
+constexpr int B_QEMPTY = 3;   // + stage
+constexpr int B_SDP = 5;
+constexpr int B_PS = 6;
+constexpr int B_DQFULL = 7;
+constexpr int B_DQFREE = 8;
+constexpr int B_DVK = 9;
+constexpr int B_FINAL = 10;
+
+constexpr uint32_t kColA = 0;
+constexpr uint32_t kColB = 128;
+constexpr uint32_t kColDV = 256;
+constexpr uint32_t kColDK = 384;
+
+struct Params {
+  int S, H, kv_len, nq, s_pad;
+  float scale, scale_log2;
+  const float* lse2_pad;    // (B, H, s_pad): LSE * log2(e), +inf padding
+  const float* delta_pad;   // (B, H, s_pad): rowsum(dO*O), 0 padding
+  float* dq_acc;            // (B, S, H, D) fp32, zeroed by the caller
+  // dK / dV output: bf16 strided tensors, or fp32 accumulators when acc != 0
+  int acc;
+  __nv_bfloat16* dk;
+  int64_t dks_b, dks_s, dks_h;
+  __nv_bfloat16* dv;
+  int64_t dvs_b, dvs_s, dvs_h;
+  float* dk_acc;            // (B, kv_len, H, D) fp32
+  float* dv_acc;
+  RopeArgs rope;            // rope.pos == nullptr: no rotation
+};
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void bulk_load(void* dst, const void* src,
+                                          uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void red_add_v4(float* addr, float a, float b,
+                                           float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr),
+               "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
+// Writes one 128-value fp32 row held in registers to a dK/dV destination.
+__device__ __forceinline__ void store_row(const Params& p, bool is_dk, int b,
+                                          int key, int h, float* v) {
+  if (p.acc) {
+    float* dst = (is_dk ? p.dk_acc : p.dv_acc) +
+                 (((int64_t)b * p.kv_len + key) * p.H + h) * 128;
+    float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+    for (int c = 0; c < 32; ++c) {
+      float4 o = d4[c];
+      o.x += v[4 * c + 0];
+      o.y += v[4 * c + 1];
+      o.z += v[4 * c + 2];
+      o.w += v[4 * c + 3];
+      d4[c] = o;
+    }
+  } else {
+    __nv_bfloat16* dst =
+        is_dk ? p.dk + (int64_t)b * p.dks_b + (int64_t)key * p.dks_s +
+                    (int64_t)h * p.dks_h
+              : p.dv + (int64_t)b * p.dvs_b + (int64_t)key * p.dvs_s +
+                    (int64_t)h * p.dvs_h;
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      uint4 o;
+      o.x = pack_bf16(v[8 * c + 0], v[8 * c + 1]);
+      o.y = pack_bf16(v[8 * c + 2], v[8 * c + 3]);
+      o.z = pack_bf16(v[8 * c + 4], v[8 * c + 5]);
+      o.w = pack_bf16(v[8 * c + 6], v[8 * c + 7]);
+      d4[c] = o;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
+                const __grid_constant__ CUtensorMap tm_k,
+                const __grid_constant__ CUtensorMap tm_v,
+                const __grid_constant__ CUtensorMap tm_do, Params p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc);
+  volatile int* abort_flag =
+      reinterpret_cast<volatile int*>(smem + kOffMisc + 4);
+  // The layout needs a 1024-byte aligned window (SWIZZLE_128B atoms).
+  if ((smem_u32(smem) & 1023u) != 0) {
+    if (threadIdx.x == 0) report_status(2 /* FA_ERR_UNSUPPORTED */);
+    return;
+  }
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const int kv_tile = blockIdx.x;
+  const int h = blockIdx.y;
+  const int b = blockIdx.z;
+  const int nq = p.nq;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[B_KV], 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars[B_QFULL + s], 1);
+      mbar_init(&bars[B_QEMPTY + s], 1);
+    }
+    mbar_init(&bars[B_SDP], 1);
+    mbar_init(&bars[B_PS], 128);
+    mbar_init(&bars[B_DQFULL], 1);
+    mbar_init(&bars[B_DQFREE], 128);
+    mbar_init(&bars[B_DVK], 1);
+    mbar_init(&bars[B_FINAL], 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int64_t lse_row0 = ((int64_t)b * p.H + h) * p.s_pad;
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      tma_prefetch_desc(&tm_do);
+      const int krow = kv_tile * kRows;
+      mbar_arrive_expect_tx(&bars[B_KV], 2 * kTileBytes);
+      tma_load_4d(smem + kOffK, &tm_k, &bars[B_KV], 0, krow, h, b);
+      tma_load_4d(smem + kOffK + kBlkBytes, &tm_k, &bars[B_KV], 64, krow, h, b);
+      tma_load_4d(smem + kOffV, &tm_v, &bars[B_KV], 0, krow, h, b);
+      tma_load_4d(smem + kOffV + kBlkBytes, &tm_v, &bars[B_KV], 64, krow, h, b);
+      bool ok = true;
+      for (int i = 0; i < nq; ++i) {
+        const int st = i & 1, n = i >> 1;
+        if (*abort_flag) break;
+        if (i >= 2 && !(ok = mbar_wait(&bars[B_QEMPTY + st], (n - 1) & 1)))
+          break;
+        const int qrow = i * kRows;
+        uint64_t* bar = &bars[B_QFULL + st];
+        mbar_arrive_expect_tx(bar, 2 * kTileBytes + 1024);
+        uint8_t* qd = smem + kOffQ + st * kTileBytes;
+        uint8_t* dd = smem + kOffDO + st * kTileBytes;
+        tma_load_4d(qd, &tm_q, bar, 0, qrow, h, b);
+        tma_load_4d(qd + kBlkBytes, &tm_q, bar, 64, qrow, h, b);
+        tma_load_4d(dd, &tm_do, bar, 0, qrow, h, b);
+        tma_load_4d(dd + kBlkBytes, &tm_do, bar, 64, qrow, h, b);
+        bulk_load(smem + kOffLse + st * 512, p.lse2_pad + lse_row0 + qrow, 512,
+                  bar);
+        bulk_load(smem + kOffDelta + st * 512, p.delta_pad + lse_row0 + qrow,
+                  512, bar);
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else if (warp == 9) {
+    // ----------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdKK = idesc_bf16(128, 128, false, false);
+      constexpr uint32_t kIdKM = idesc_bf16(128, 128, false, true);
+      constexpr uint32_t kIdMM = idesc_bf16(128, 128, true, true);
+      const uint32_t k_base = smem_u32(smem + kOffK);
+      const uint32_t v_base = smem_u32(smem + kOffV);
+      const uint32_t ds_base = smem_u32(smem + kOffDS);
+      bool ok = mbar_wait(&bars[B_KV], 0);
+      tc_fence_after();
+      for (int i = 0; ok && i < nq; ++i) {
+        const int st = i & 1, n = i >> 1;
+        if (*abort_flag) { ok = false; break; }
+        if (!(ok = mbar_wait(&bars[B_QFULL + st], n & 1))) break;
+        const uint32_t q_base = smem_u32(smem + kOffQ + st * kTileBytes);
+        const uint32_t do_base = smem_u32(smem + kOffDO + st * kTileBytes);
+        // S^T_i = K Q_i^T -> A   (A was read by dV/dK of step i-1)
+        if (i > 0 && !(ok = mbar_wait(&bars[B_DVK], (i - 1) & 1))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_ss(tmem + kColA, kmajor_desc(k_base, kk, kBlkBytes),
+                  kmajor_desc(q_base, kk, kBlkBytes), kIdKK, kk > 0);
+        // dP^T_i = V dO_i^T -> B   (B held dQ_{i-1} until it was drained)
+        if (i > 0 && !(ok = mbar_wait(&bars[B_DQFREE], (i - 1) & 1))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_ss(tmem + kColB, kmajor_desc(v_base, kk, kBlkBytes),
+                  kmajor_desc(do_base, kk, kBlkBytes), kIdKK, kk > 0);
+        umma_commit(&bars[B_SDP]);
+        if (!(ok = mbar_wait(&bars[B_PS], i & 1))) break;
+        tc_fence_after();
+        // dV += P^T dO_i ; dK += dS^T Q_i   (A operands from TMEM)
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_ts(tmem + kColDV, tmem + kColA + kk * 8,
+                  mnmajor_desc(do_base, kk, kBlkBytes), kIdKM,
+                  (i > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_ts(tmem + kColDK, tmem + kColA + 64 + kk * 8,
+                  mnmajor_desc(q_base, kk, kBlkBytes), kIdKM,
+                  (i > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&bars[B_DVK]);
+        umma_commit(&bars[B_QEMPTY + st]);
+        // dQ_i = dS_i K -> B   (dS from shared memory, query-major view)
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_ss(tmem + kColB, mnmajor_desc(ds_base, kk, kBlkBytes),
+                  mnmajor_desc(k_base, kk, kBlkBytes), kIdMM, kk > 0);
+        umma_commit(&bars[B_DQFULL]);
+      }
+      if (!ok) *abort_flag = 1;
+      umma_commit(&bars[B_FINAL]);
+      mbar_wait(&bars[B_FINAL], 0);
+    }
+  } else if (warp < 4) {
+    // ----------------------------------------- softmax backward (key rows)
+    const int key_in_tile = warp * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const uint32_t t_a = tmem + lane_off + kColA;
+    const uint32_t t_b = tmem + lane_off + kColB;
+    uint8_t* ds_row = smem + kOffDS;
+    const float sl2 = p.scale_log2;
+    bool ok = true;
+    for (int i = 0; i < nq; ++i) {
+      const int st = i & 1, n = i >> 1;
+      if (__any_sync(0xffffffffu, *abort_flag != 0)) { ok = false; break; }
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_SDP], i & 1));
+      if (!ok) break;
+      // the LSE / Delta slices arrived with Q_i (already complete here)
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_QFULL + st], n & 1));
+      if (!ok) break;
+      tc_fence_after();
+      const float* lse2 = reinterpret_cast<const float*>(smem + kOffLse + st * 512);
+      const float* dlt = reinterpret_cast<const float*>(smem + kOffDelta + st * 512);
+      uint32_t pr[128];
+      tmem_ld32(t_a + 0, pr);
+      tmem_ld32(t_a + 32, pr + 32);
+      tmem_ld32(t_a + 64, pr + 64);
+      tmem_ld32(t_a + 96, pr + 96);
+      tmem_wait_ld();
+      float* pv = reinterpret_cast<float*>(pr);
+#pragma unroll
+      for (int c = 0; c < 128; ++c) pv[c] = fast_exp2(fmaf(pv[c], sl2, -lse2[c]));
+#pragma unroll
+      for (int cb = 0; cb < 4; ++cb) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u)
+          pk[u] = pack_bf16(pv[cb * 32 + 2 * u], pv[cb * 32 + 2 * u + 1]);
+        tmem_st16(t_a + cb * 16, pk);
+      }
+#pragma unroll
+      for (int cb = 0; cb < 4; ++cb) {
+        uint32_t dr[32];
+        tmem_ld32(t_b + cb * 32, dr);
+        tmem_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+          const int c0 = cb * 32 + 2 * u;
+          const float d0 = pv[c0] * (__uint_as_float(dr[2 * u]) - dlt[c0]);
+          const float d1 =
+              pv[c0 + 1] * (__uint_as_float(dr[2 * u + 1]) - dlt[c0 + 1]);
+          pk[u] = pack_bf16(d0, d1);
+        }
+        tmem_st16(t_a + 64 + cb * 16, pk);
+        // dS^T row -> shared memory: queries [32cb, 32cb+32) are 16-byte
+        // chunks 4*(cb&1) .. +3 of swizzle block cb>>1.
+        uint8_t* blk = ds_row + (cb >> 1) * kBlkBytes;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const uint32_t off = sw128_offset(key_in_tile, (cb & 1) * 4 + u);
+          *reinterpret_cast<uint4*>(blk + off) =
+              make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+        }
+      }
+      tmem_wait_st();
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&bars[B_PS]);
+    }
+    // dV epilogue
+    if (ok && __all_sync(0xffffffffu, mbar_wait(&bars[B_FINAL], 0)) &&
+        !__any_sync(0xffffffffu, *abort_flag != 0)) {
+      tc_fence_after();
+      uint32_t r[128];
+      const uint32_t t_dv = tmem + lane_off + kColDV;
+      tmem_ld32(t_dv + 0, r);
+      tmem_ld32(t_dv + 32, r + 32);
+      tmem_ld32(t_dv + 64, r + 64);
+      tmem_ld32(t_dv + 96, r + 96);
+      tmem_wait_ld();
+      const int key = kv_tile * kRows + key_in_tile;
+      if (key < p.kv_len) store_row(p, false, b, key, h, reinterpret_cast<float*>(r));
+    } else {
+      *abort_flag = 1;
+    }
+  } else {
+    // ------------------------------------------ dQ drain (query rows)
+    const int sub = warp & 3;
+    const int row_in_tile = sub * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(sub * 32) << 16;
+    const uint32_t t_b = tmem + lane_off + kColB;
+    bool ok = true;
+    for (int i = 0; i < nq; ++i) {
+      if (__any_sync(0xffffffffu, *abort_flag != 0)) { ok = false; break; }
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_DQFULL], i & 1));
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t r[128];
+      tmem_ld32(t_b + 0, r);
+      tmem_ld32(t_b + 32, r + 32);
+      tmem_ld32(t_b + 64, r + 64);
+      tmem_ld32(t_b + 96, r + 96);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&bars[B_DQFREE]);
+      const int q = i * kRows + row_in_tile;
+      if (q < p.S) {
+        float* dst = p.dq_acc + (((int64_t)b * p.S + q) * p.H + h) * 128;
+        const float* v = reinterpret_cast<const float*>(r);
+#pragma unroll
+        for (int c = 0; c < 32; ++c)
+          red_add_v4(dst + 4 * c, v[4 * c], v[4 * c + 1], v[4 * c + 2],
+                     v[4 * c + 3]);
+      }
+    }
+    // dK epilogue: scale, inverse rotation (when the op owns the RoPE)
+    if (ok && __all_sync(0xffffffffu, mbar_wait(&bars[B_FINAL], 0)) &&
+        !__any_sync(0xffffffffu, *abort_flag != 0)) {
+      tc_fence_after();
+      uint32_t r[128];
+      const uint32_t t_dk = tmem + lane_off + kColDK;
+      tmem_ld32(t_dk + 0, r);
+      tmem_ld32(t_dk + 32, r + 32);
+      tmem_ld32(t_dk + 64, r + 64);
+      tmem_ld32(t_dk + 96, r + 96);
+      tmem_wait_ld();
+      const int key = kv_tile * kRows + row_in_tile;
+      float* v = reinterpret_cast<float*>(r);
+#pragma unroll
+      for (int c = 0; c < 128; ++c) v[c] *= p.scale;
+      if (key < p.kv_len) {
+        if (p.rope.pos != nullptr) rope_rotate_row128(p.rope, key, v, true);
+        store_row(p, true, b, key, h, v);
+      }
+    } else {
+      *abort_flag = 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace bwd
+
+int launch_attn_bwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
+                         const fa_tensor_t* k, const fa_tensor_t* v,
+                         const fa_tensor_t* d_o, const float* lse2_pad,
+                         const float* delta_pad, float* dq_acc,
+                         const fa_tensor_t* dk, const fa_tensor_t* dv,
+                         float* dk_acc, float* dv_acc, float scale,
+                         const fa_rope_t* rope, cudaStream_t stream) {
+  CUtensorMap tq, tk, tv, tdo;
+  int rc = make_tmap_bshd(&tq, q, sh.B, sh.S, sh.H, sh.D, 128);
+  if (!rc) rc = make_tmap_bshd(&tk, k, sh.B, kv_len, sh.H, sh.D, 128);
+  if (!rc) rc = make_tmap_bshd(&tv, v, sh.B, kv_len, sh.H, sh.D, 128);
+  if (!rc) rc = make_tmap_bshd(&tdo, d_o, sh.B, sh.S, sh.H, sh.D, 128);
+  if (rc) return rc;
+  bwd::Params p;
+  p.S = sh.S;
+  p.H = sh.H;
+  p.kv_len = kv_len;
+  p.nq = (sh.S + 127) / 128;
+  p.s_pad = p.nq * 128;
+  p.scale = scale;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.lse2_pad = lse2_pad;
+  p.delta_pad = delta_pad;
+  p.dq_acc = dq_acc;
+  p.acc = (dk_acc != nullptr) ? 1 : 0;
+  p.dk = dk ? reinterpret_cast<__nv_bfloat16*>(dk->data) : nullptr;
+  p.dks_b = dk ? dk->stride_b : 0;
+  p.dks_s = dk ? dk->stride_s : 0;
+  p.dks_h = dk ? dk->stride_h : 0;
+  p.dv = dv ? reinterpret_cast<__nv_bfloat16*>(dv->data) : nullptr;
+  p.dvs_b = dv ? dv->stride_b : 0;
+  p.dvs_s = dv ? dv->stride_s : 0;
+  p.dvs_h = dv ? dv->stride_h : 0;
+  p.dk_acc = dk_acc;
+  p.dv_acc = dv_acc;
+  p.rope = make_rope_args(rope);
+  rc = ensure_smem_attr((const void*)bwd::attn_bwd_kernel, bwd::kSmemBytes,
+                        kKernelBwdBf16);
+  if (rc) return rc;
+  dim3 grid((kv_len + 127) / 128, sh.H, sh.B);
+  bwd::attn_bwd_kernel<<<grid, bwd::kThreads, bwd::kSmemBytes, stream>>>(
+      tq, tk, tv, tdo, p);
+  return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+}
+
+}  // namespace fa

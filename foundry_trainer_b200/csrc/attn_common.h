@@ -1,0 +1,81 @@
+// attn_common.h — host-side helpers shared by the attention launchers:
+// shapes, TMA descriptor encoding for strided (B, S, H, D) tensors, and the
+// per-device shared-memory attribute cache.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/foundry_attn.h"
+
+namespace fa {
+
+struct AttnShape {
+  int B, S, H, D;
+};
+
+// Encodes a 4-D TMA descriptor over a bf16 (B, S, H, D) tensor with box
+// (64 head-dim elements, box_rows tokens, 1, 1), SWIZZLE_128B, zero fill out
+// of bounds. Returns FA_OK or an FA_ERR_* code.
+int make_tmap_bshd(CUtensorMap* map, const fa_tensor_t* t, int B, int S, int H,
+                   int D, int box_rows);
+
+// Same over an fp32 (B, S, H, D) tensor with box (32, box_rows, 1, 1).
+int make_tmap_bshd_f32(CUtensorMap* map, const fa_tensor_t* t, int B, int S,
+                       int H, int D, int box_rows);
+
+enum KernelId {
+  kKernelFwdBf16 = 0,
+  kKernelBwdBf16 = 1,
+  kKernelF32Fwd = 2,
+  kKernelF32Bwd = 3,
+  kKernelCount = 8
+};
+
+// Raises the dynamic shared-memory limit of `fn` once per (device, kernel).
+int ensure_smem_attr(const void* fn, int bytes, int kernel_id);
+
+// bf16 sm_100a kernels
+int launch_attn_fwd_bf16(const AttnShape& sh, const fa_tensor_t* q,
+                         const fa_tensor_t* k, const fa_tensor_t* v,
+                         const fa_tensor_t* o, float* lse, float scale,
+                         cudaStream_t stream);
+
+int launch_attn_bwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
+                         const fa_tensor_t* k, const fa_tensor_t* v,
+                         const fa_tensor_t* d_o, const float* lse2_pad,
+                         const float* delta_pad, float* dq_acc,
+                         const fa_tensor_t* dk, const fa_tensor_t* dv,
+                         float* dk_acc, float* dv_acc, float scale,
+                         const fa_rope_t* rope, cudaStream_t stream);
+
+// fp32 SIMT kernels (exact path)
+int launch_attn_fwd_f32(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
+                        const fa_tensor_t* k, const fa_tensor_t* v,
+                        const fa_tensor_t* o, float* lse, float scale,
+                        cudaStream_t stream);
+int launch_attn_bwd_f32(const AttnShape& sh, const fa_tensor_t* q,
+                        const fa_tensor_t* k, const fa_tensor_t* v,
+                        const fa_tensor_t* d_o, const float* lse,
+                        const float* delta, const fa_tensor_t* dq,
+                        const fa_tensor_t* dk, const fa_tensor_t* dv,
+                        float scale, cudaStream_t stream);
+
+// elementwise helpers (misc.cu)
+// delta[b,h,s] = sum_d dO*O over rows s < s_pad (0 for s >= S); when lse2 is
+// non-null also lse2[b,h,s] = lse*log2(e) (+inf for s >= S).
+int launch_bwd_delta(int dtype, const AttnShape& sh, const fa_tensor_t* o,
+                     const fa_tensor_t* d_o, const float* lse, float* delta,
+                     float* lse2, int s_pad, cudaStream_t stream);
+int launch_rope(int dtype, const AttnShape& sh, const fa_tensor_t* x,
+                const fa_tensor_t* y, const fa_rope_t* rope, int inverse,
+                int pos_offset, cudaStream_t stream);
+int launch_cast_f32(int dtype, const AttnShape& sh, const float* x,
+                    const fa_tensor_t* y, float alpha, const fa_rope_t* rope,
+                    int pos_offset, cudaStream_t stream);
+int launch_lse_merge(int dtype, const AttnShape& sh, float* o_acc,
+                     float* lse_acc, const fa_tensor_t* o_blk,
+                     const float* lse_blk, int first, cudaStream_t stream);
+
+}  // namespace fa

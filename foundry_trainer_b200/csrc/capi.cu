@@ -1,0 +1,480 @@
+// capi.cu — the extern "C" entry points of include/foundry_attn.h:
+// argument validation, workspace carving, and the launch sequences of the
+// forward, backward and sequence-shard building blocks.
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <utility>
+#include <vector>
+
+#include "attn_common.h"
+#include "rope.cuh"
+#include "sm100_ptx.cuh"
+
+namespace fa {
+
+__device__ int g_device_status = 0;
+
+// ------------------------------------------------------------ TMA encoding
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+static std::once_flag g_encode_once;
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn,
+                                cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  return g_encode;
+}
+
+static int encode_bshd(CUtensorMap* map, const fa_tensor_t* t, int B, int S,
+                       int H, int D, int box_rows, CUtensorMapDataType dt,
+                       int esize, int box_inner) {
+  auto enc = encode_fn();
+  if (!enc) return FA_ERR_LAUNCH;
+  if (t->stride_d != 1) return FA_ERR_ALIGNMENT;
+  // Size-1 modes may carry any stride; give them a legal one.
+  int64_t ss = t->stride_s, sh = t->stride_h, sb = t->stride_b;
+  if (H == 1) sh = (int64_t)D;
+  if (S == 1) ss = (int64_t)D * H;
+  if (B == 1) sb = (int64_t)S * ss;
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)H, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)(ss * esize), (cuuint64_t)(sh * esize),
+                           (cuuint64_t)(sb * esize)};
+  for (int i = 0; i < 3; ++i)
+    if (strides[i] % 16 != 0 || strides[i] >= (1ull << 40)) return FA_ERR_ALIGNMENT;
+  if (reinterpret_cast<uintptr_t>(t->data) % 16 != 0) return FA_ERR_ALIGNMENT;
+  cuuint32_t box[4] = {(cuuint32_t)box_inner, (cuuint32_t)box_rows, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, dt, 4, t->data, dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? FA_OK : FA_ERR_ALIGNMENT;
+}
+
+int make_tmap_bshd(CUtensorMap* map, const fa_tensor_t* t, int B, int S, int H,
+                   int D, int box_rows) {
+  return encode_bshd(map, t, B, S, H, D, box_rows,
+                     CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 64);
+}
+
+int make_tmap_bshd_f32(CUtensorMap* map, const fa_tensor_t* t, int B, int S,
+                       int H, int D, int box_rows) {
+  return encode_bshd(map, t, B, S, H, D, box_rows,
+                     CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, 32);
+}
+
+// ------------------------------------------------- per-device attributes
+static std::atomic<int> g_attr_done[64][kKernelCount];
+
+int ensure_smem_attr(const void* fn, int bytes, int kernel_id) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return FA_ERR_NO_DEVICE;
+  if (g_attr_done[dev][kernel_id].load(std::memory_order_acquire)) return FA_OK;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           bytes) != cudaSuccess)
+    return FA_ERR_LAUNCH;
+  g_attr_done[dev][kernel_id].store(1, std::memory_order_release);
+  return FA_OK;
+}
+
+RopeArgs make_rope_args(const fa_rope_t* rope, int round_bf16, int pos_offset) {
+  RopeArgs r;
+  std::memset(&r, 0, sizeof(r));
+  if (rope == nullptr) return r;
+  r.pos = rope->pos;
+  r.n_axes = rope->n_axes;
+  r.axis_dim = rope->axis_dim;
+  r.round_bf16 = round_bf16;
+  r.pos_offset = pos_offset;
+  const int half = rope->axis_dim / 2;
+  for (int a = 0; a < rope->n_axes; ++a)
+    for (int j = 0; j < half; ++j)
+      r.inv_freq[a * half + j] = (float)std::pow(
+          (double)rope->theta, -2.0 * (double)j / (double)rope->axis_dim);
+  return r;
+}
+
+// --------------------------------------------------------------- validation
+static int check_sm100() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return FA_ERR_NO_DEVICE;
+  int major = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) !=
+      cudaSuccess)
+    return FA_ERR_NO_DEVICE;
+  return major == 10 ? FA_OK : FA_ERR_NO_DEVICE;
+}
+
+static int check_tensor(const fa_tensor_t* t, int esize, bool tma) {
+  if (t == nullptr || t->data == nullptr) return FA_ERR_INVALID_ARG;
+  if (t->stride_d != 1) return FA_ERR_ALIGNMENT;
+  if (tma) {
+    if (reinterpret_cast<uintptr_t>(t->data) % 16 != 0) return FA_ERR_ALIGNMENT;
+  } else if (reinterpret_cast<uintptr_t>(t->data) % esize != 0) {
+    return FA_ERR_ALIGNMENT;
+  }
+  return FA_OK;
+}
+
+static int check_shape(int dtype, int B, int S, int H, int D) {
+  if (dtype != FA_DTYPE_F32 && dtype != FA_DTYPE_BF16) return FA_ERR_UNSUPPORTED;
+  if (B <= 0 || S <= 0 || H <= 0 || D <= 0) return FA_ERR_INVALID_ARG;
+  if (D != 128) return FA_ERR_UNSUPPORTED;
+  if ((int64_t)B * S * H * D >= (int64_t)1 << 40) return FA_ERR_TOO_LARGE;
+  if (B > 65535 || H > 65535) return FA_ERR_TOO_LARGE;
+  return FA_OK;
+}
+
+static int check_rope(const fa_rope_t* rope, int D) {
+  if (rope == nullptr) return FA_OK;
+  if (rope->pos == nullptr) return FA_ERR_INVALID_ARG;
+  if (rope->n_axes <= 0 || rope->axis_dim <= 0 || (rope->axis_dim & 1))
+    return FA_ERR_UNSUPPORTED;
+  if (rope->n_axes * rope->axis_dim != D) return FA_ERR_UNSUPPORTED;
+  if (rope->n_axes * rope->axis_dim / 2 > kMaxRopeFreqs) return FA_ERR_UNSUPPORTED;
+  if (!(rope->theta > 0.f)) return FA_ERR_INVALID_ARG;
+  return FA_OK;
+}
+
+static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+static fa_tensor_t contiguous_view(void* p, int S, int H, int D) {
+  fa_tensor_t t;
+  t.data = p;
+  t.stride_d = 1;
+  t.stride_h = D;
+  t.stride_s = (int64_t)H * D;
+  t.stride_b = (int64_t)S * H * D;
+  return t;
+}
+
+// ------------------------------------------- per-kernel CUDA-event timing
+// Optional measurement hook: when enabled, the main forward / backward kernel
+// launches are bracketed by CUDA events on their own stream so a benchmark can
+// read each kernel's device time without a profiler. One device per process.
+struct TimerSlot {
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> pairs;
+  size_t used = 0;
+};
+static std::mutex g_timer_mu;
+static std::atomic<int> g_timing{0};
+static TimerSlot g_slots[FA_TIMER_COUNT];
+
+static cudaEvent_t timer_begin(int id, cudaStream_t st) {
+  if (!g_timing.load(std::memory_order_relaxed)) return nullptr;
+  std::lock_guard<std::mutex> lk(g_timer_mu);
+  TimerSlot& s = g_slots[id];
+  if (s.used == s.pairs.size()) {
+    cudaEvent_t a, b;
+    if (cudaEventCreate(&a) != cudaSuccess) return nullptr;
+    if (cudaEventCreate(&b) != cudaSuccess) {
+      cudaEventDestroy(a);
+      return nullptr;
+    }
+    s.pairs.emplace_back(a, b);
+  }
+  auto& pr = s.pairs[s.used++];
+  cudaEventRecord(pr.first, st);
+  return pr.second;
+}
+
+static void timer_end(cudaEvent_t stop, cudaStream_t st) {
+  if (stop != nullptr) cudaEventRecord(stop, st);
+}
+
+#define FA_TRY(expr)            \
+  do {                          \
+    int _rc = (expr);           \
+    if (_rc != FA_OK) return _rc; \
+  } while (0)
+
+}  // namespace fa
+
+using namespace fa;
+
+extern "C" {
+
+const char* fa_status_string(int status) {
+  switch (status) {
+    case FA_OK: return "ok";
+    case FA_ERR_INVALID_ARG: return "invalid argument";
+    case FA_ERR_UNSUPPORTED: return "unsupported dtype, head_dim or rope layout";
+    case FA_ERR_ALIGNMENT: return "stride or pointer violates TMA alignment (16 B)";
+    case FA_ERR_LAUNCH: return "CUDA launch or runtime call failed";
+    case FA_ERR_DEVICE_TIMEOUT: return "device-side bounded wait expired";
+    case FA_ERR_WORKSPACE: return "workspace missing or too small";
+    case FA_ERR_NO_DEVICE: return "no sm_100 device current";
+    case FA_ERR_TOO_LARGE: return "size beyond addressing limits";
+    default: return "unknown status";
+  }
+}
+
+int fa_abi_version(void) { return FA_ABI_VERSION; }
+
+const char* fa_build_info(void) {
+  return "foundry_attn sm_100a (tcgen05/TMEM/TMA bf16 path, fp32 SIMT path)";
+}
+
+int fa_device_status(void) {
+  if (cudaDeviceSynchronize() != cudaSuccess) return FA_ERR_LAUNCH;
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_device_status, sizeof(int)) != cudaSuccess)
+    return FA_ERR_LAUNCH;
+  const int zero = 0;
+  if (v != 0 && cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int)) != cudaSuccess)
+    return FA_ERR_LAUNCH;
+  return v;
+}
+
+size_t fa_fwd_workspace_bytes(int dtype, int B, int S, int H, int D,
+                              const fa_rope_t* rope) {
+  if (rope == nullptr) return 0;
+  const size_t es = dtype == FA_DTYPE_BF16 ? 2 : 4;
+  return 2 * align256((size_t)B * S * H * D * es);
+}
+
+int fa_fwd(int dtype, int B, int S, int H, int D, const fa_tensor_t* q,
+           const fa_tensor_t* k, const fa_tensor_t* v, const fa_tensor_t* o,
+           float* lse, float scale, const fa_rope_t* rope, void* workspace,
+           size_t workspace_bytes, void* stream) {
+  FA_TRY(check_shape(dtype, B, S, H, D));
+  FA_TRY(check_rope(rope, D));
+  if (!(scale > 0.f) || !std::isfinite(scale)) return FA_ERR_INVALID_ARG;
+  const bool bf = dtype == FA_DTYPE_BF16;
+  const int es = bf ? 2 : 4;
+  FA_TRY(check_tensor(q, es, bf));
+  FA_TRY(check_tensor(k, es, bf));
+  FA_TRY(check_tensor(v, es, bf));
+  FA_TRY(check_tensor(o, es, true));
+  if (lse == nullptr) return FA_ERR_INVALID_ARG;
+  FA_TRY(check_sm100());
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const AttnShape sh{B, S, H, D};
+  fa_tensor_t qr = *q, kr = *k;
+  if (rope != nullptr) {
+    const size_t need = fa_fwd_workspace_bytes(dtype, B, S, H, D, rope);
+    if (workspace == nullptr || workspace_bytes < need) return FA_ERR_WORKSPACE;
+    uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+    qr = contiguous_view(ws, S, H, D);
+    kr = contiguous_view(ws + need / 2, S, H, D);
+    FA_TRY(launch_rope(dtype, sh, q, &qr, rope, 0, 0, st));
+    FA_TRY(launch_rope(dtype, sh, k, &kr, rope, 0, 0, st));
+  }
+  cudaEvent_t stop = timer_begin(FA_TIMER_FWD, st);
+  const int rc = bf ? launch_attn_fwd_bf16(sh, &qr, &kr, v, o, lse, scale, st)
+                    : launch_attn_fwd_f32(sh, S, &qr, &kr, v, o, lse, scale, st);
+  timer_end(stop, st);
+  return rc;
+}
+
+// workspace: [q_rot | k_rot] (rope) | lse2_pad | delta_pad | dq_acc (bf16) ;
+//            [q_rot | k_rot | dq_rot | dk_rot] (rope) | delta (f32)
+size_t fa_bwd_workspace_bytes(int dtype, int B, int S, int H, int D,
+                              const fa_rope_t* rope, int deterministic) {
+  (void)deterministic;
+  const size_t n = (size_t)B * S * H * D;
+  if (dtype == FA_DTYPE_BF16) {
+    const size_t s_pad = (size_t)((S + 127) / 128) * 128;
+    size_t total = 0;
+    if (rope) total += 2 * align256(n * 2);
+    total += 2 * align256((size_t)B * H * s_pad * 4);
+    total += align256(n * 4);
+    return total;
+  }
+  size_t total = 0;
+  if (rope) total += 4 * align256(n * 4);
+  total += align256((size_t)B * H * S * 4);
+  return total;
+}
+
+int fa_bwd(int dtype, int B, int S, int H, int D, const fa_tensor_t* q,
+           const fa_tensor_t* k, const fa_tensor_t* v, const fa_tensor_t* o,
+           const fa_tensor_t* d_o, const float* lse, const fa_tensor_t* dq,
+           const fa_tensor_t* dk, const fa_tensor_t* dv, float scale,
+           const fa_rope_t* rope, int deterministic, void* workspace,
+           size_t workspace_bytes, void* stream) {
+  FA_TRY(check_shape(dtype, B, S, H, D));
+  FA_TRY(check_rope(rope, D));
+  if (!(scale > 0.f) || !std::isfinite(scale)) return FA_ERR_INVALID_ARG;
+  const bool bf = dtype == FA_DTYPE_BF16;
+  const int es = bf ? 2 : 4;
+  for (const fa_tensor_t* t : {q, k, v, d_o}) FA_TRY(check_tensor(t, es, bf));
+  for (const fa_tensor_t* t : {o, dq, dk, dv}) FA_TRY(check_tensor(t, es, true));
+  if (lse == nullptr) return FA_ERR_INVALID_ARG;
+  if (bf && deterministic) return FA_ERR_UNSUPPORTED;
+  FA_TRY(check_sm100());
+  const size_t need = fa_bwd_workspace_bytes(dtype, B, S, H, D, rope, deterministic);
+  if (workspace == nullptr || workspace_bytes < need) return FA_ERR_WORKSPACE;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const AttnShape sh{B, S, H, D};
+  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+  const size_t n = (size_t)B * S * H * D;
+  fa_tensor_t qr = *q, kr = *k;
+  if (bf) {
+    if (rope) {
+      qr = contiguous_view(ws, S, H, D);
+      ws += align256(n * 2);
+      kr = contiguous_view(ws, S, H, D);
+      ws += align256(n * 2);
+      FA_TRY(launch_rope(dtype, sh, q, &qr, rope, 0, 0, st));
+      FA_TRY(launch_rope(dtype, sh, k, &kr, rope, 0, 0, st));
+    }
+    const int s_pad = ((S + 127) / 128) * 128;
+    float* lse2 = reinterpret_cast<float*>(ws);
+    ws += align256((size_t)B * H * s_pad * 4);
+    float* delta = reinterpret_cast<float*>(ws);
+    ws += align256((size_t)B * H * s_pad * 4);
+    float* dq_acc = reinterpret_cast<float*>(ws);
+    FA_TRY(launch_bwd_delta(dtype, sh, o, d_o, lse, delta, lse2, s_pad, st));
+    if (cudaMemsetAsync(dq_acc, 0, n * 4, st) != cudaSuccess) return FA_ERR_LAUNCH;
+    cudaEvent_t stop = timer_begin(FA_TIMER_BWD, st);
+    const int rc = launch_attn_bwd_bf16(sh, S, &qr, &kr, v, d_o, lse2, delta,
+                                        dq_acc, dk, dv, nullptr, nullptr, scale,
+                                        rope, st);
+    timer_end(stop, st);
+    FA_TRY(rc);
+    return launch_cast_f32(dtype, sh, dq_acc, dq, scale, rope, 0, st);
+  }
+  // fp32 path
+  fa_tensor_t dqr = *dq, dkr = *dk;
+  if (rope) {
+    qr = contiguous_view(ws, S, H, D);
+    ws += align256(n * 4);
+    kr = contiguous_view(ws, S, H, D);
+    ws += align256(n * 4);
+    dqr = contiguous_view(ws, S, H, D);
+    ws += align256(n * 4);
+    dkr = contiguous_view(ws, S, H, D);
+    ws += align256(n * 4);
+    FA_TRY(launch_rope(dtype, sh, q, &qr, rope, 0, 0, st));
+    FA_TRY(launch_rope(dtype, sh, k, &kr, rope, 0, 0, st));
+  }
+  float* delta = reinterpret_cast<float*>(ws);
+  FA_TRY(launch_bwd_delta(dtype, sh, o, d_o, lse, delta, nullptr, S, st));
+  cudaEvent_t stop = timer_begin(FA_TIMER_BWD, st);
+  const int rc = launch_attn_bwd_f32(sh, &qr, &kr, v, d_o, lse, delta, &dqr,
+                                     &dkr, dv, scale, st);
+  timer_end(stop, st);
+  FA_TRY(rc);
+  if (rope) {
+    FA_TRY(launch_rope(dtype, sh, &dqr, dq, rope, 1, 0, st));
+    FA_TRY(launch_rope(dtype, sh, &dkr, dk, rope, 1, 0, st));
+  }
+  return FA_OK;
+}
+
+int fa_rope_apply(int dtype, int B, int S, int H, int D, const fa_tensor_t* x,
+                  const fa_tensor_t* y, const fa_rope_t* rope, int inverse,
+                  void* stream) {
+  FA_TRY(check_shape(dtype, B, S, H, D));
+  if (rope == nullptr) return FA_ERR_INVALID_ARG;
+  FA_TRY(check_rope(rope, D));
+  const int es = dtype == FA_DTYPE_BF16 ? 2 : 4;
+  FA_TRY(check_tensor(x, es, false));
+  FA_TRY(check_tensor(y, es, false));
+  FA_TRY(check_sm100());
+  return launch_rope(dtype, AttnShape{B, S, H, D}, x, y, rope, inverse, 0,
+                     reinterpret_cast<cudaStream_t>(stream));
+}
+
+int fa_fwd_partial(int dtype, int B, int S, int kv_len, int H, int D,
+                   const fa_tensor_t* q, const fa_tensor_t* k,
+                   const fa_tensor_t* v, const fa_tensor_t* o_blk,
+                   float* lse_blk, float scale, void* stream) {
+  FA_TRY(check_shape(dtype, B, S, H, D));
+  if (kv_len <= 0) return FA_ERR_INVALID_ARG;
+  const bool bf = dtype == FA_DTYPE_BF16;
+  const int es = bf ? 2 : 4;
+  for (const fa_tensor_t* t : {q, k, v, o_blk}) FA_TRY(check_tensor(t, es, bf));
+  if (lse_blk == nullptr) return FA_ERR_INVALID_ARG;
+  FA_TRY(check_sm100());
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const AttnShape sh{B, S, H, D};
+  if (bf) {
+    if (kv_len != S) return FA_ERR_UNSUPPORTED;  // equal shards on this path
+    return launch_attn_fwd_bf16(sh, q, k, v, o_blk, lse_blk, scale, st);
+  }
+  return launch_attn_fwd_f32(sh, kv_len, q, k, v, o_blk, lse_blk, scale, st);
+}
+
+int fa_lse_merge(int dtype, int B, int S, int H, int D, float* o_acc,
+                 float* lse_acc, const fa_tensor_t* o_blk,
+                 const float* lse_blk, int first, void* stream) {
+  FA_TRY(check_shape(dtype, B, S, H, D));
+  if (!o_acc || !lse_acc || !lse_blk) return FA_ERR_INVALID_ARG;
+  FA_TRY(check_tensor(o_blk, dtype == FA_DTYPE_BF16 ? 2 : 4, false));
+  FA_TRY(check_sm100());
+  return launch_lse_merge(dtype, AttnShape{B, S, H, D}, o_acc, lse_acc, o_blk,
+                          lse_blk, first, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int fa_bwd_delta(int dtype, int B, int S, int H, int D, const fa_tensor_t* o,
+                 const fa_tensor_t* d_o, float* delta, void* stream) {
+  FA_TRY(check_shape(dtype, B, S, H, D));
+  const int es = dtype == FA_DTYPE_BF16 ? 2 : 4;
+  FA_TRY(check_tensor(o, es, false));
+  FA_TRY(check_tensor(d_o, es, false));
+  if (delta == nullptr) return FA_ERR_INVALID_ARG;
+  FA_TRY(check_sm100());
+  return launch_bwd_delta(dtype, AttnShape{B, S, H, D}, o, d_o, nullptr, delta,
+                          nullptr, S, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int fa_bwd_partial(int dtype, int B, int S, int kv_len, int H, int D,
+                   const fa_tensor_t* q, const fa_tensor_t* k,
+                   const fa_tensor_t* v, const fa_tensor_t* d_o,
+                   const float* lse, const float* delta, float* dq_acc,
+                   float* dk_acc, float* dv_acc, float scale, void* stream) {
+  (void)q; (void)k; (void)v; (void)d_o; (void)lse; (void)delta; (void)dq_acc;
+  (void)dk_acc; (void)dv_acc; (void)scale; (void)stream; (void)kv_len;
+  FA_TRY(check_shape(dtype, B, S, H, D));
+  return FA_ERR_UNSUPPORTED;  // sequence-shard backward: not built yet
+}
+
+int fa_cast_f32(int dtype, int B, int S, int H, int D, const float* x,
+                const fa_tensor_t* y, float alpha, const fa_rope_t* rope,
+                void* stream) {
+  FA_TRY(check_shape(dtype, B, S, H, D));
+  FA_TRY(check_rope(rope, D));
+  if (x == nullptr) return FA_ERR_INVALID_ARG;
+  FA_TRY(check_tensor(y, dtype == FA_DTYPE_BF16 ? 2 : 4, false));
+  FA_TRY(check_sm100());
+  return launch_cast_f32(dtype, AttnShape{B, S, H, D}, x, y, alpha, rope, 0,
+                         reinterpret_cast<cudaStream_t>(stream));
+}
+
+int fa_timing_enable(int on) {
+  g_timing.store(on ? 1 : 0, std::memory_order_relaxed);
+  return FA_OK;
+}
+
+int fa_timing_read(int kernel, double* total_ms, int* launches) {
+  if (kernel < 0 || kernel >= FA_TIMER_COUNT || !total_ms || !launches)
+    return FA_ERR_INVALID_ARG;
+  std::lock_guard<std::mutex> lk(g_timer_mu);
+  TimerSlot& s = g_slots[kernel];
+  double total = 0.0;
+  for (size_t i = 0; i < s.used; ++i) {
+    if (cudaEventSynchronize(s.pairs[i].second) != cudaSuccess) return FA_ERR_LAUNCH;
+    float ms = 0.f;
+    if (cudaEventElapsedTime(&ms, s.pairs[i].first, s.pairs[i].second) != cudaSuccess)
+      return FA_ERR_LAUNCH;
+    total += ms;
+  }
+  *total_ms = total;
+  *launches = (int)s.used;
+  s.used = 0;
+  return FA_OK;
+}
+
+}  // extern "C"

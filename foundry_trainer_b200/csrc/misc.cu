@@ -1,0 +1,244 @@
+// misc.cu — memory-bound helpers around the attention kernels:
+//   * backward prologue: Delta = rowsum(dO * O) and the padded LSE*log2(e)
+//     table the bf16 backward streams with each Q tile;
+//   * axial RoPE apply / inverse (the reference's apply_rope, lib.rs:122-129);
+//   * fp32 -> compute-dtype cast with scale and inverse rotation (dQ finish);
+//   * log-sum-exp merge of two partial attention results (sequence shards).
+// All are one pass over their rows; one warp per (b, s, h) row, lane l owns
+// head-dim columns {l, l+32, l+64, l+96} so loads are coalesced and the
+// rotate-half partner of column d (d +- 16 inside a 32-wide axis segment) is
+// lane l ^ 16 holding the same slot.
+#include "attn_common.h"
+#include "rope.cuh"
+#include "sm100_ptx.cuh"
+
+namespace fa {
+namespace misc {
+
+constexpr int kWarps = 8;
+
+template <typename T>
+__device__ __forceinline__ float ld_elem(const T* p);
+template <>
+__device__ __forceinline__ float ld_elem<float>(const float* p) { return *p; }
+template <>
+__device__ __forceinline__ float ld_elem<__nv_bfloat16>(const __nv_bfloat16* p) {
+  return __bfloat162float(*p);
+}
+template <typename T>
+__device__ __forceinline__ void st_elem(T* p, float v);
+template <>
+__device__ __forceinline__ void st_elem<float>(float* p, float v) { *p = v; }
+template <>
+__device__ __forceinline__ void st_elem<__nv_bfloat16>(__nv_bfloat16* p, float v) {
+  *p = __float2bfloat16_rn(v);
+}
+
+struct TView {
+  const void* p;
+  int64_t sb, ss, sh;
+};
+struct TOut {
+  void* p;
+  int64_t sb, ss, sh;
+};
+
+// rows ordered (b, h, s) with s in [0, s_pad): writes delta (and lse2) rows
+template <typename T>
+__global__ void delta_kernel(TView o, TView d_o, const float* lse, float* delta,
+                             float* lse2, int S, int H, int s_pad, int B) {
+  const int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= (int64_t)B * H * s_pad) return;
+  const int s = (int)(row % s_pad);
+  const int64_t bh = row / s_pad;
+  const int h = (int)(bh % H), b = (int)(bh / H);
+  float acc = 0.f;
+  if (s < S) {
+    const T* po = reinterpret_cast<const T*>(o.p) + b * o.sb + s * o.ss + h * o.sh;
+    const T* pd = reinterpret_cast<const T*>(d_o.p) + b * d_o.sb + s * d_o.ss + h * d_o.sh;
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+      acc = fmaf(ld_elem<T>(po + lane + 32 * a), ld_elem<T>(pd + lane + 32 * a), acc);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) {
+    delta[row] = acc;
+    if (lse2 != nullptr)
+      lse2[row] = (s < S) ? lse[bh * S + s] * 1.4426950408889634f : INFINITY;
+  }
+}
+
+// One warp per row: y = rot(x) (or the inverse), fp32 math, axis_dim == 32.
+template <typename Tin, typename Tout>
+__global__ void rope_warp_kernel(TView x, TOut y, RopeArgs r, int S, int H,
+                                 int B, float alpha, int inverse) {
+  const int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= (int64_t)B * S * H) return;
+  const int h = (int)(row % H);
+  const int64_t bs = row / H;
+  const int s = (int)(bs % S), b = (int)(bs / S);
+  const Tin* px = reinterpret_cast<const Tin*>(x.p) + b * x.sb + s * x.ss + h * x.sh;
+  Tout* py = reinterpret_cast<Tout*>(y.p) + b * y.sb + s * y.ss + h * y.sh;
+  float v[4];
+#pragma unroll
+  for (int a = 0; a < 4; ++a) v[a] = ld_elem<Tin>(px + lane + 32 * a) * alpha;
+  if (r.pos != nullptr) {
+    const float* pos = r.pos + (int64_t)(s + r.pos_offset) * r.n_axes;
+    const int j = lane & 15;
+    const bool first = lane < 16;
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+      const float other = __shfl_xor_sync(0xffffffffu, v[a], 16);
+      if (a < r.n_axes) {
+        const float f = __fmul_rn(pos[a], r.inv_freq[a * 16 + j]);
+        float sn, cs;
+        sincosf(f, &sn, &cs);
+        if (r.round_bf16) {
+          cs = round_bf16_f(cs);
+          sn = round_bf16_f(sn);
+        }
+        // forward: y1 = x1 c - x2 s, y2 = x2 c + x1 s; inverse: transpose
+        const float sgn = (first != (inverse != 0)) ? -1.f : 1.f;
+        v[a] = __fadd_rn(__fmul_rn(v[a], cs), __fmul_rn(sgn * other, sn));
+      }
+    }
+  }
+#pragma unroll
+  for (int a = 0; a < 4; ++a) st_elem<Tout>(py + lane + 32 * a, v[a]);
+}
+
+// Generic thread-per-row rotation for other axis layouts.
+template <typename Tin, typename Tout>
+__global__ void rope_row_kernel(TView x, TOut y, RopeArgs r, int S, int H,
+                                int B, float alpha, int inverse) {
+  const int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= (int64_t)B * S * H) return;
+  const int h = (int)(row % H);
+  const int64_t bs = row / H;
+  const int s = (int)(bs % S), b = (int)(bs / S);
+  const Tin* px = reinterpret_cast<const Tin*>(x.p) + b * x.sb + s * x.ss + h * x.sh;
+  Tout* py = reinterpret_cast<Tout*>(y.p) + b * y.sb + s * y.ss + h * y.sh;
+  float v[128];
+  for (int d = 0; d < 128; ++d) v[d] = ld_elem<Tin>(px + d) * alpha;
+  if (r.pos != nullptr) rope_rotate_row128(r, s, v, inverse != 0);
+  for (int d = 0; d < 128; ++d) st_elem<Tout>(py + d, v[d]);
+}
+
+// (o_acc, lse_acc) <- merge with (o_blk, lse_blk); rows (b, s, h).
+template <typename T>
+__global__ void lse_merge_kernel(float* o_acc, float* lse_acc, TView o_blk,
+                                 const float* lse_blk, int S, int H, int B,
+                                 int first) {
+  const int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= (int64_t)B * S * H) return;
+  const int h = (int)(row % H);
+  const int64_t bs = row / H;
+  const int s = (int)(bs % S), b = (int)(bs / S);
+  const int64_t li = ((int64_t)b * H + h) * S + s;
+  const T* pb = reinterpret_cast<const T*>(o_blk.p) + b * o_blk.sb + s * o_blk.ss + h * o_blk.sh;
+  float* pa = o_acc + row * 128;
+  const float lb = lse_blk[li];
+  if (first) {
+#pragma unroll
+    for (int a = 0; a < 4; ++a) pa[lane + 32 * a] = ld_elem<T>(pb + lane + 32 * a);
+    if (lane == 0) lse_acc[li] = lb;
+    return;
+  }
+  const float la = lse_acc[li];
+  const float mx = fmaxf(la, lb);
+  const float wa = expf(la - mx), wb = expf(lb - mx);
+  const float inv = 1.f / (wa + wb);
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+    const int d = lane + 32 * a;
+    pa[d] = (pa[d] * wa + ld_elem<T>(pb + d) * wb) * inv;
+  }
+  __syncwarp();
+  if (lane == 0) lse_acc[li] = mx + logf(wa + wb);
+}
+
+TView tview(const fa_tensor_t* t) { return TView{t->data, t->stride_b, t->stride_s, t->stride_h}; }
+TOut tout(const fa_tensor_t* t) { return TOut{t->data, t->stride_b, t->stride_s, t->stride_h}; }
+
+}  // namespace misc
+
+int launch_bwd_delta(int dtype, const AttnShape& sh, const fa_tensor_t* o,
+                     const fa_tensor_t* d_o, const float* lse, float* delta,
+                     float* lse2, int s_pad, cudaStream_t stream) {
+  const int64_t rows = (int64_t)sh.B * sh.H * s_pad;
+  const dim3 grid((unsigned)((rows + misc::kWarps - 1) / misc::kWarps));
+  if (dtype == FA_DTYPE_BF16)
+    misc::delta_kernel<__nv_bfloat16><<<grid, 32 * misc::kWarps, 0, stream>>>(
+        misc::tview(o), misc::tview(d_o), lse, delta, lse2, sh.S, sh.H, s_pad, sh.B);
+  else
+    misc::delta_kernel<float><<<grid, 32 * misc::kWarps, 0, stream>>>(
+        misc::tview(o), misc::tview(d_o), lse, delta, lse2, sh.S, sh.H, s_pad, sh.B);
+  return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+}
+
+static int launch_rope_generic(int dtype_in, int dtype_out, const AttnShape& sh,
+                               const misc::TView& x, const misc::TOut& y,
+                               const RopeArgs& r, float alpha, int inverse,
+                               cudaStream_t stream) {
+  const int64_t rows = (int64_t)sh.B * sh.S * sh.H;
+  const bool warp_path = (r.pos == nullptr) || (r.axis_dim == 32 && r.n_axes <= 4);
+  if (warp_path) {
+    const dim3 grid((unsigned)((rows + misc::kWarps - 1) / misc::kWarps));
+    const int nt = 32 * misc::kWarps;
+#define FA_ROPE_W(TI, TO) \
+  misc::rope_warp_kernel<TI, TO><<<grid, nt, 0, stream>>>(x, y, r, sh.S, sh.H, sh.B, alpha, inverse)
+    if (dtype_in == FA_DTYPE_BF16 && dtype_out == FA_DTYPE_BF16) FA_ROPE_W(__nv_bfloat16, __nv_bfloat16);
+    else if (dtype_in == FA_DTYPE_F32 && dtype_out == FA_DTYPE_BF16) FA_ROPE_W(float, __nv_bfloat16);
+    else if (dtype_in == FA_DTYPE_F32 && dtype_out == FA_DTYPE_F32) FA_ROPE_W(float, float);
+    else FA_ROPE_W(__nv_bfloat16, float);
+#undef FA_ROPE_W
+  } else {
+    const dim3 grid((unsigned)((rows + 127) / 128));
+#define FA_ROPE_R(TI, TO) \
+  misc::rope_row_kernel<TI, TO><<<grid, 128, 0, stream>>>(x, y, r, sh.S, sh.H, sh.B, alpha, inverse)
+    if (dtype_in == FA_DTYPE_BF16 && dtype_out == FA_DTYPE_BF16) FA_ROPE_R(__nv_bfloat16, __nv_bfloat16);
+    else if (dtype_in == FA_DTYPE_F32 && dtype_out == FA_DTYPE_BF16) FA_ROPE_R(float, __nv_bfloat16);
+    else if (dtype_in == FA_DTYPE_F32 && dtype_out == FA_DTYPE_F32) FA_ROPE_R(float, float);
+    else FA_ROPE_R(__nv_bfloat16, float);
+#undef FA_ROPE_R
+  }
+  return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+}
+
+int launch_rope(int dtype, const AttnShape& sh, const fa_tensor_t* x,
+                const fa_tensor_t* y, const fa_rope_t* rope, int inverse,
+                int pos_offset, cudaStream_t stream) {
+  const RopeArgs r = make_rope_args(rope, dtype == FA_DTYPE_BF16 ? 1 : 0, pos_offset);
+  return launch_rope_generic(dtype, dtype, sh, misc::tview(x), misc::tout(y), r,
+                             1.f, inverse, stream);
+}
+
+int launch_cast_f32(int dtype, const AttnShape& sh, const float* x,
+                    const fa_tensor_t* y, float alpha, const fa_rope_t* rope,
+                    int pos_offset, cudaStream_t stream) {
+  const RopeArgs r = make_rope_args(rope, dtype == FA_DTYPE_BF16 ? 1 : 0, pos_offset);
+  const int64_t D = sh.D;
+  misc::TView xv{x, (int64_t)sh.S * sh.H * D, (int64_t)sh.H * D, D};
+  return launch_rope_generic(FA_DTYPE_F32, dtype, sh, xv, misc::tout(y), r,
+                             alpha, 1, stream);
+}
+
+int launch_lse_merge(int dtype, const AttnShape& sh, float* o_acc,
+                     float* lse_acc, const fa_tensor_t* o_blk,
+                     const float* lse_blk, int first, cudaStream_t stream) {
+  const int64_t rows = (int64_t)sh.B * sh.S * sh.H;
+  const dim3 grid((unsigned)((rows + misc::kWarps - 1) / misc::kWarps));
+  if (dtype == FA_DTYPE_BF16)
+    misc::lse_merge_kernel<__nv_bfloat16><<<grid, 32 * misc::kWarps, 0, stream>>>(
+        o_acc, lse_acc, misc::tview(o_blk), lse_blk, sh.S, sh.H, sh.B, first);
+  else
+    misc::lse_merge_kernel<float><<<grid, 32 * misc::kWarps, 0, stream>>>(
+        o_acc, lse_acc, misc::tview(o_blk), lse_blk, sh.S, sh.H, sh.B, first);
+  return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+}
+
+}  // namespace fa

@@ -1,0 +1,72 @@
+// rope.cuh — axial rotary embedding arithmetic, the reference's
+// rope_tables_dtype + rope_rotate_half + apply_rope
+// (crates/foundry-spike/src/lib.rs:77-129):
+//   for axis a (segment [a*dim_a, (a+1)*dim_a)) and j < dim_a/2:
+//     f   = pos[a] * theta^(-2j/dim_a)                 (fp32)
+//     c,s = cos f, sin f in fp32, rounded to the compute dtype (lib.rs:101-103)
+//     y1  = x1*c + (-x2)*s,  y2 = x2*c + x1*s          (x1 = x[j], x2 = x[j+dim_a/2])
+// with products and the sum each rounded in fp32 (no fused multiply-add), as
+// the reference's separate broadcast_mul and add do. The inverse (gradient of
+// apply_rope) is the transposed rotation: x1 = y1*c + y2*s, x2 = y2*c - y1*s.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "../../include/foundry_attn.h"
+
+namespace fa {
+
+constexpr int kMaxRopeFreqs = 64;  // n_axes * dim_a / 2 for head_dim 128
+
+struct RopeArgs {
+  const float* pos;  // (S, n_axes) fp32, nullptr: no rotation
+  int n_axes;
+  int axis_dim;
+  int round_bf16;    // 1: round cos/sin to bf16 (compute dtype bf16)
+  int pos_offset;    // token index offset into pos (sequence shards)
+  float inv_freq[kMaxRopeFreqs];  // theta^(-2j/dim_a), j < dim_a/2
+};
+
+// Host: builds the kernel argument block (inv_freq in fp32, correctly rounded
+// from double, as the reference's fp32 powf of an exact exponent).
+RopeArgs make_rope_args(const fa_rope_t* rope, int round_bf16 = 1,
+                        int pos_offset = 0);
+
+__device__ __forceinline__ float round_bf16_f(float x) {
+  return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+// Rotates (inverse == false) or un-rotates one 128-wide row in place.
+__device__ __forceinline__ void rope_rotate_row128(const RopeArgs& r,
+                                                   int token, float* v,
+                                                   bool inverse) {
+  const int half = r.axis_dim >> 1;
+  const float* pos = r.pos + (int64_t)(token + r.pos_offset) * r.n_axes;
+#pragma unroll 1
+  for (int a = 0; a < r.n_axes; ++a) {
+    const float pa = pos[a];
+    float* seg = v + a * r.axis_dim;
+#pragma unroll 4
+    for (int j = 0; j < half; ++j) {
+      const float f = __fmul_rn(pa, r.inv_freq[a * half + j]);
+      float s, c;
+      sincosf(f, &s, &c);
+      if (r.round_bf16) {
+        c = round_bf16_f(c);
+        s = round_bf16_f(s);
+      }
+      const float x1 = seg[j];
+      const float x2 = seg[j + half];
+      if (!inverse) {
+        seg[j] = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(-x2, s));
+        seg[j + half] = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+      } else {
+        seg[j] = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+        seg[j + half] = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(-x1, s));
+      }
+    }
+  }
+}
+
+}  // namespace fa

@@ -1,0 +1,144 @@
+"""Tensor-level calls into the C ABI (PyTorch supplies device memory and streams).
+
+Layouts follow the reference op: (S, H, D) per sequence as in
+crates/foundry-spike/src/lib.rs:134, or batched (B, S, H, D). Any strides are
+accepted as long as the head dimension is contiguous and the other strides
+are 16-byte multiples (the TMA rule); nothing is copied to make inputs
+contiguous.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import _lib
+from ._lib import FA_DTYPE_BF16, FA_DTYPE_F32, check, fa_rope_t, fa_tensor_t
+
+ROPE_AXES = (32, 32, 32, 32)  # lib.rs:20
+ROPE_THETA = 10000.0          # lib.rs:21
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    if t.dtype == torch.bfloat16:
+        return FA_DTYPE_BF16
+    if t.dtype == torch.float32:
+        return FA_DTYPE_F32
+    raise TypeError(f"unsupported dtype {t.dtype}: the op computes in bf16 or f32")
+
+
+def as_bshd(t: torch.Tensor) -> torch.Tensor:
+    """(S,H,D) -> (1,S,H,D) view; (B,S,H,D) unchanged."""
+    if t.dim() == 3:
+        return t.unsqueeze(0)
+    if t.dim() == 4:
+        return t
+    raise ValueError(f"expected (S,H,D) or (B,S,H,D), got shape {tuple(t.shape)}")
+
+
+def desc(t: torch.Tensor) -> fa_tensor_t:
+    t4 = as_bshd(t)
+    if not t4.is_cuda:
+        raise ValueError("tensor must live on a CUDA device")
+    sb, ss, sh, sd = t4.stride()
+    return fa_tensor_t(t4.data_ptr(), sb, ss, sh, sd)
+
+
+def _stream_ptr(stream: Optional[torch.cuda.Stream]) -> int:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+@dataclass
+class Rope:
+    """Axial RoPE descriptor: per-token positions (S, n_axes) and theta.
+
+    Mirrors rope_tables_dtype (lib.rs:77-105); the tables are never
+    materialised, the kernels evaluate cos/sin from the positions.
+    """
+    pos: torch.Tensor              # (S, n_axes) float32 on the device
+    axis_dim: int = 32
+    theta: float = ROPE_THETA
+
+    def c_struct(self) -> fa_rope_t:
+        p = self.pos
+        if p.dtype != torch.float32 or not p.is_contiguous() or p.dim() != 2:
+            raise ValueError("rope positions must be a contiguous (S, n_axes) float32 tensor")
+        return fa_rope_t(p.data_ptr(), p.shape[1], self.axis_dim, self.theta)
+
+
+def _ref(x):
+    return C.byref(x) if x is not None else None
+
+
+def default_scale(d: int) -> float:
+    return 1.0 / math.sqrt(d)  # lib.rs:138
+
+
+def attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: Optional[float] = None,
+             rope: Optional[Rope] = None, out: Optional[torch.Tensor] = None,
+             lse: Optional[torch.Tensor] = None, stream=None):
+    """O and fp32 LSE (B, H, S) of softmax(Q K^T * scale) V."""
+    q4, k4, v4 = as_bshd(q), as_bshd(k), as_bshd(v)
+    B, S, H, D = q4.shape
+    if k4.shape != q4.shape or v4.shape != q4.shape:
+        raise ValueError("q, k, v must share one shape")
+    if not (q.dtype == k.dtype == v.dtype):
+        raise TypeError("q, k, v must share one dtype")
+    dt = _dtype_code(q)
+    if out is None:
+        out = torch.empty_like(q)
+    if lse is None:
+        lse = torch.empty((B, H, S), device=q.device, dtype=torch.float32)
+    scale = default_scale(D) if scale is None else float(scale)
+    lib = _lib.load()
+    rc_rope = rope.c_struct() if rope is not None else None
+    ws_bytes = lib.fa_fwd_workspace_bytes(dt, B, S, H, D, _ref(rc_rope))
+    ws = torch.empty(ws_bytes, device=q.device, dtype=torch.uint8) if ws_bytes else None
+    dq_, dk_, dv_, do_ = desc(q4), desc(k4), desc(v4), desc(as_bshd(out))
+    check(lib.fa_fwd(dt, B, S, H, D, C.byref(dq_), C.byref(dk_), C.byref(dv_), C.byref(do_),
+                     lse.data_ptr(), scale, _ref(rc_rope), ws.data_ptr() if ws is not None else None,
+                     ws_bytes, _stream_ptr(stream)), "fa_fwd")
+    return out, lse
+
+
+def attn_bwd(q, k, v, o, d_o, lse, *, scale: Optional[float] = None, rope: Optional[Rope] = None,
+             deterministic: bool = False, dq=None, dk=None, dv=None, stream=None):
+    """dQ, dK, dV of the op (w.r.t. pre-rotation q/k when rope is given)."""
+    q4 = as_bshd(q)
+    B, S, H, D = q4.shape
+    dt = _dtype_code(q)
+    dq = torch.empty_like(q) if dq is None else dq
+    dk = torch.empty_like(k) if dk is None else dk
+    dv = torch.empty_like(v) if dv is None else dv
+    scale = default_scale(D) if scale is None else float(scale)
+    lib = _lib.load()
+    rc_rope = rope.c_struct() if rope is not None else None
+    ws_bytes = lib.fa_bwd_workspace_bytes(dt, B, S, H, D, _ref(rc_rope), int(deterministic))
+    ws = torch.empty(max(ws_bytes, 1), device=q.device, dtype=torch.uint8)
+    ds = [desc(x) for x in (q, k, v, o, d_o, dq, dk, dv)]
+    check(lib.fa_bwd(dt, B, S, H, D, *[C.byref(x) for x in ds[:5]], lse.data_ptr(),
+                     *[C.byref(x) for x in ds[5:]], scale, _ref(rc_rope), int(deterministic),
+                     ws.data_ptr(), ws_bytes, _stream_ptr(stream)), "fa_bwd")
+    return dq, dk, dv
+
+
+def rope_apply(x: torch.Tensor, rope: Rope, *, inverse: bool = False, out=None, stream=None):
+    """The reference's apply_rope (lib.rs:122-129) on the device."""
+    x4 = as_bshd(x)
+    B, S, H, D = x4.shape
+    out = torch.empty_like(x) if out is None else out
+    r = rope.c_struct()
+    dx, dy = desc(x), desc(out)
+    check(_lib.load().fa_rope_apply(_dtype_code(x), B, S, H, D, C.byref(dx), C.byref(dy),
+                                    C.byref(r), int(inverse), _stream_ptr(stream)),
+          "fa_rope_apply")
+    return out
+
+
+def device_status() -> int:
+    """Reads and clears the device status word (0 when no bounded wait expired)."""
+    return int(_lib.load().fa_device_status())

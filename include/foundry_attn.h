@@ -1,0 +1,196 @@
+/*
+ * foundry_attn.h — C ABI of the B200 (sm_100a) joint text+image attention op.
+ *
+ * This is the drop-in boundary for foundry-trainer's attention custom op
+ * `AttnBwd` (crates/foundry-spike/src/lib.rs:151-264). A host binding (the Rust
+ * FFI crate described in INTEGRATION.md, the C++ mirror in foundry_attn_op.hpp,
+ * or the Python ctypes mirror) calls these entry points; nothing here uses
+ * torch or any other framework type.
+ *
+ * Conventions (all entry points):
+ *   - Tensors are (B, S, H, D) with arbitrary element strides (fa_tensor_t);
+ *     the reference's op is the B == 1 case with (S, H, D) inputs (lib.rs:134).
+ *     The head-dim stride must be 1; other strides times the element size must
+ *     be multiples of 16 bytes and base pointers 16-byte aligned (TMA rules).
+ *   - The caller owns every buffer, including workspaces; nothing allocates.
+ *   - Calls are asynchronous and ordered on `stream` (a cudaStream_t; NULL is
+ *     the legacy default stream).
+ *   - Errors are status codes (FA_OK == 0); nothing throws across the ABI.
+ *     fa_status_string() names a code. Device-side bounded waits that expire
+ *     report FA_ERR_DEVICE_TIMEOUT through fa_device_status().
+ *   - Reentrant. The only global state is a per-device, call-once cache of the
+ *     driver entry point used to encode TMA descriptors, and the device status
+ *     word.
+ */
+#ifndef FOUNDRY_ATTN_H
+#define FOUNDRY_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FA_ABI_VERSION 1
+
+/* status codes */
+#define FA_OK 0
+#define FA_ERR_INVALID_ARG 1     /* null pointer, non-positive size, bad scale */
+#define FA_ERR_UNSUPPORTED 2     /* dtype / head_dim / rope layout not supported */
+#define FA_ERR_ALIGNMENT 3       /* stride or base pointer violates the TMA rules */
+#define FA_ERR_LAUNCH 4          /* a CUDA launch or runtime call failed */
+#define FA_ERR_DEVICE_TIMEOUT 5  /* a device-side bounded wait expired */
+#define FA_ERR_WORKSPACE 6       /* workspace missing or too small */
+#define FA_ERR_NO_DEVICE 7       /* no sm_100 device current */
+#define FA_ERR_TOO_LARGE 8       /* size beyond the kernel's addressing limits */
+
+/* element types; the reference's compute dtypes are f32 and bf16 (lib.rs:139-147) */
+#define FA_DTYPE_F32 0
+#define FA_DTYPE_BF16 1
+
+/* A strided (B, S, H, D) device tensor. Strides are in elements. */
+typedef struct {
+  void* data;
+  int64_t stride_b;
+  int64_t stride_s;
+  int64_t stride_h;
+  int64_t stride_d;
+} fa_tensor_t;
+
+/*
+ * Axial rotary embedding, the reference's rope_tables_dtype + apply_rope
+ * (lib.rs:77-129): per token a position vector of n_axes floats; axis a owns
+ * head-dim segment [a*axis_dim, (a+1)*axis_dim); frequency j < axis_dim/2 is
+ * theta^(-2j/axis_dim); rotate-half inside each segment. cos/sin are computed
+ * in fp32 and rounded to the compute dtype before use, as the reference does.
+ * `pos` is a device pointer to a (S, n_axes) fp32 array shared by the batch.
+ * Supported: n_axes * axis_dim == D, axis_dim even.
+ */
+typedef struct {
+  const float* pos;
+  int n_axes;
+  int axis_dim;
+  float theta;
+} fa_rope_t;
+
+/*
+ * Forward. Replaces AttnBwd::cuda_fwd (lib.rs:189-214) / attn_fwd
+ * (lib.rs:133-149): O = softmax(Q K^T * scale) V, non-causal, no mask.
+ * Also writes the per-row log-sum-exp `lse` (fp32, contiguous (B, H, S),
+ * natural log of sum exp(scaled scores)) that fa_bwd consumes; the reference
+ * recomputes it instead (lib.rs:232-238).
+ * If `rope` is non-NULL, q and k are pre-rotation and the rotation is applied
+ * inside the op (the reference applies it before the op, lib.rs:326-358).
+ * `workspace` (may be NULL when fa_fwd_workspace_bytes() returns 0) holds the
+ * rotated keys and must stay untouched until the matching fa_bwd returns.
+ */
+int fa_fwd(int dtype, int B, int S, int H, int D,
+           const fa_tensor_t* q, const fa_tensor_t* k, const fa_tensor_t* v,
+           const fa_tensor_t* o, float* lse, float scale, const fa_rope_t* rope,
+           void* workspace, size_t workspace_bytes, void* stream);
+
+size_t fa_fwd_workspace_bytes(int dtype, int B, int S, int H, int D,
+                              const fa_rope_t* rope);
+
+/*
+ * Backward. Replaces AttnBwd::bwd (lib.rs:216-263): given q, k, v, the
+ * forward output o, its gradient d_o and the saved lse, writes dq, dk, dv
+ * (w.r.t. the pre-rotation q/k when `rope` is non-NULL).
+ * `deterministic` != 0 requests bit-identical results across repeats
+ * (the reference's stability gate, bin/stability.rs:175-190); the f32 path is
+ * always deterministic.
+ * `workspace` must hold fa_bwd_workspace_bytes(); it carries the fp32 dQ
+ * accumulator and the per-row softmax-gradient term.
+ */
+int fa_bwd(int dtype, int B, int S, int H, int D,
+           const fa_tensor_t* q, const fa_tensor_t* k, const fa_tensor_t* v,
+           const fa_tensor_t* o, const fa_tensor_t* d_o, const float* lse,
+           const fa_tensor_t* dq, const fa_tensor_t* dk, const fa_tensor_t* dv,
+           float scale, const fa_rope_t* rope, int deterministic,
+           void* workspace, size_t workspace_bytes, void* stream);
+
+size_t fa_bwd_workspace_bytes(int dtype, int B, int S, int H, int D,
+                              const fa_rope_t* rope, int deterministic);
+
+/*
+ * Standalone rotation, the reference's apply_rope (lib.rs:122-129) for
+ * callers that rotate outside the op: y = x*cos + rotate_half(x)*sin per axis
+ * segment, fp32 arithmetic, result in `dtype`. `inverse` != 0 applies the
+ * transposed rotation (the gradient of apply_rope). x and y may alias.
+ */
+int fa_rope_apply(int dtype, int B, int S, int H, int D, const fa_tensor_t* x,
+                  const fa_tensor_t* y, const fa_rope_t* rope, int inverse,
+                  void* stream);
+
+/*
+ * Sequence-parallel (ring) building blocks. They have no counterpart in the
+ * reference, which is single-GPU (SURVEY: no collectives anywhere); they let a
+ * host driver rotate K/V shards between ranks and fold each block into the
+ * local result.
+ *
+ * fa_fwd_partial: like fa_fwd on one K/V block (kv_len keys, rows indexed
+ *   by the block), writing an un-normalised-free partial (o_blk, lse_blk); the
+ *   caller merges blocks with fa_lse_merge. q rows are S; keys are kv_len.
+ * fa_lse_merge: (o_acc, lse_acc) <- merge((o_acc, lse_acc), (o_blk, lse_blk))
+ *   with o_acc fp32 (B,S,H,D) contiguous and o_blk in `dtype`; first != 0
+ *   initialises from the block.
+ * fa_bwd_partial: one K/V block of the backward: accumulates scale*dS*K into
+ *   the fp32 dq_acc (B,S,H,D contiguous) and adds the block's dK, dV into the
+ *   fp32 dk_acc, dv_acc (B,kv_len,H,D contiguous). `delta` is the per-row
+ *   rowsum(dO*O) (B,H,S) from fa_bwd_delta.
+ * fa_bwd_delta: delta[b,h,s] = sum_d dO*O in fp32.
+ * fa_cast_f32: y(dtype) = x(fp32 contiguous B,S,H,D) * alpha, with the inverse
+ *   rotation applied when rope is non-NULL.
+ */
+int fa_fwd_partial(int dtype, int B, int S, int kv_len, int H, int D,
+                   const fa_tensor_t* q, const fa_tensor_t* k,
+                   const fa_tensor_t* v, const fa_tensor_t* o_blk,
+                   float* lse_blk, float scale, void* stream);
+int fa_lse_merge(int dtype, int B, int S, int H, int D, float* o_acc,
+                 float* lse_acc, const fa_tensor_t* o_blk,
+                 const float* lse_blk, int first, void* stream);
+int fa_bwd_delta(int dtype, int B, int S, int H, int D, const fa_tensor_t* o,
+                 const fa_tensor_t* d_o, float* delta, void* stream);
+int fa_bwd_partial(int dtype, int B, int S, int kv_len, int H, int D,
+                   const fa_tensor_t* q, const fa_tensor_t* k,
+                   const fa_tensor_t* v, const fa_tensor_t* d_o,
+                   const float* lse, const float* delta, float* dq_acc,
+                   float* dk_acc, float* dv_acc, float scale, void* stream);
+int fa_cast_f32(int dtype, int B, int S, int H, int D, const float* x,
+                const fa_tensor_t* y, float alpha, const fa_rope_t* rope,
+                void* stream);
+
+/*
+ * Measurement hooks (no counterpart in the reference, which only wall-clocks
+ * whole steps, bin/throughput.rs:868-873). While enabled, every launch of the
+ * main forward (FA_TIMER_FWD) and backward (FA_TIMER_BWD) kernel is bracketed
+ * by CUDA events on its stream. fa_timing_read synchronises on the recorded
+ * events, returns the summed device time and launch count since the last
+ * read, and resets them. Intended for one device per process.
+ */
+#define FA_TIMER_FWD 0
+#define FA_TIMER_BWD 1
+#define FA_TIMER_COUNT 2
+int fa_timing_enable(int on);
+int fa_timing_read(int kernel, double* total_ms, int* launches);
+
+/* Human-readable name of a status code. Never NULL. */
+const char* fa_status_string(int status);
+
+/*
+ * Reads and clears the device status word of the current device that the
+ * kernels set when a bounded wait expires (0 when clean). Synchronises the
+ * current device.
+ */
+int fa_device_status(void);
+
+/* ABI version (FA_ABI_VERSION) and a build string. */
+int fa_abi_version(void);
+const char* fa_build_info(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FOUNDRY_ATTN_H */

@@ -1,0 +1,66 @@
+"""fp32 path parity: the exact SIMT kernels against the oracle at 1e-4
+max-relative error (the reference's fp32 tolerance, docs/TESTING.md:17),
+config C1 and the reference's fp32 fixture."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import attn_oracle as orc
+from tests.helpers import assert_close, run_op
+
+pytestmark = pytest.mark.gpu
+
+
+def test_fp32_fixture_replay(golden_dir):
+    g = dict(np.load(golden_dir / "attn_fixture_fp32.npz"))
+    for blk in ("double", "single"):
+        q, k, v, dout = (torch.from_numpy(g[f"{blk}_{n}"]).cuda() for n in ("q", "k", "v", "dout"))
+        o, lse, dq, dk, dv = run_op(q, k, v, dout)
+        assert_close({"o": o[0], "dq": dq[0], "dk": dk[0], "dv": dv[0]},
+                     {"o": g[f"{blk}_attn"], "dq": g[f"{blk}_dq"], "dk": g[f"{blk}_dk"],
+                      "dv": g[f"{blk}_dv"]}, 1e-4, blk)
+
+
+@pytest.mark.parametrize("with_rope", [False, True])
+def test_c1_parity(with_rope):
+    from foundry_trainer_b200 import configs, ops
+    cfg = configs.CONFIGS["c1"]
+    q, k, v, d_o = configs.make_inputs(cfg)
+    pos = configs.positions(cfg.txt, cfg.grid)
+    rope = ops.Rope(pos.cuda()) if with_rope else None
+    o, lse, dq, dk, dv = run_op(*(t.cuda() for t in (q, k, v, d_o)), rope=rope)
+    ro, rlse, rdq, rdk, rdv = orc.attn_fwd_bwd_bshd(q.numpy(), k.numpy(), v.numpy(), d_o.numpy(),
+                                                    "f32", rope_pos=pos.numpy() if with_rope else None)
+    assert_close({"o": o, "lse": lse, "dq": dq, "dk": dk, "dv": dv},
+                 {"o": ro, "lse": rlse, "dq": rdq, "dk": rdk, "dv": rdv}, 1e-4, "c1")
+
+
+def test_fp32_rope_inside_op_fixture(golden_dir):
+    from foundry_trainer_b200 import ops
+    g = dict(np.load(golden_dir / "attn_rope_fixture_fp32.npz"))
+    q, k, v, dout = (torch.from_numpy(g[n]).cuda() for n in ("q", "k", "v", "dout"))
+    rope = ops.Rope(torch.from_numpy(g["pos"]).cuda())
+    o, lse, dq, dk, dv = run_op(q, k, v, dout, rope=rope)
+    assert_close({"o": o[0], "dq": dq[0], "dk": dk[0], "dv": dv[0]},
+                 {"o": g["o"], "dq": g["dq"], "dk": g["dk"], "dv": g["dv"]}, 1e-4, "rope fixture")
+
+
+def test_fp32_ragged_and_batched():
+    rng = np.random.default_rng(3)
+    for B, S, H in ((1, 1, 1), (2, 33, 3), (1, 97, 2)):
+        q, k, v, d_o = (rng.standard_normal((B, S, H, 128)).astype(np.float32) for _ in range(4))
+        o, lse, dq, dk, dv = run_op(*(torch.from_numpy(x).cuda() for x in (q, k, v, d_o)))
+        ro, rlse, rdq, rdk, rdv = orc.attn_fwd_bwd_bshd(q, k, v, d_o, "f32")
+        assert_close({"o": o, "lse": lse, "dq": dq, "dk": dk, "dv": dv},
+                     {"o": ro, "lse": rlse, "dq": rdq, "dk": rdk, "dv": rdv}, 1e-4, f"{B},{S},{H}")
+
+
+def test_fp32_bit_identical_repeats():
+    from foundry_trainer_b200 import configs
+    cfg = configs.CONFIGS["c1"]
+    q, k, v, d_o = (t.cuda() for t in configs.make_inputs(cfg))
+    first = run_op(q, k, v, d_o)
+    for _ in range(2):
+        again = run_op(q, k, v, d_o)
+        for a, b in zip(first, again):
+            assert np.array_equal(a, b)

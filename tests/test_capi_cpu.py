@@ -1,0 +1,77 @@
+"""The C ABI library loads and exports every entry point the header declares;
+host-side validation answers without a GPU (no kernel is launched here)."""
+import ctypes as C
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _declared():
+    text = (ROOT / "include" / "foundry_attn.h").read_text()
+    return sorted(set(re.findall(r"^\s*(?:int|size_t|const char\*)\s+(fa_\w+)\s*\(", text, re.M)))
+
+
+def test_header_declarations_found():
+    names = _declared()
+    assert "fa_fwd" in names and "fa_bwd" in names and len(names) >= 12
+
+
+def test_library_exports_every_declared_symbol():
+    from foundry_trainer_b200 import _lib
+    lib = _lib.load()
+    for name in _declared():
+        assert hasattr(lib, name), name
+    assert set(_declared()) <= set(_lib.SIGNATURES)
+
+
+def test_status_strings_and_version():
+    from foundry_trainer_b200 import _lib
+    lib = _lib.load()
+    assert lib.fa_abi_version() == 1
+    for code in range(0, 9):
+        assert lib.fa_status_string(code)
+    assert _lib.status_string(0) == "ok"
+
+
+def test_validation_rejects_bad_arguments_without_a_gpu():
+    from foundry_trainer_b200 import _lib
+    lib = _lib.load()
+    t = _lib.fa_tensor_t(None, 0, 0, 0, 1)
+    # null tensors
+    rc = lib.fa_fwd(_lib.FA_DTYPE_BF16, 1, 16, 1, 128, C.byref(t), C.byref(t), C.byref(t),
+                    C.byref(t), None, 0.1, None, None, 0, None)
+    assert rc == _lib.FA_ERR_INVALID_ARG
+    # unsupported head dim and dtype
+    assert lib.fa_fwd(_lib.FA_DTYPE_BF16, 1, 16, 1, 64, None, None, None, None, None, 0.1, None,
+                      None, 0, None) == _lib.FA_ERR_UNSUPPORTED
+    assert lib.fa_fwd(7, 1, 16, 1, 128, None, None, None, None, None, 0.1, None, None, 0,
+                      None) == _lib.FA_ERR_UNSUPPORTED
+    # non-positive sizes
+    assert lib.fa_bwd(_lib.FA_DTYPE_BF16, 0, 16, 1, 128, None, None, None, None, None, None, None,
+                      None, None, 0.1, None, 0, None, 0, None) == _lib.FA_ERR_INVALID_ARG
+    # a rotation whose axes do not cover the head dim
+    r = _lib.fa_rope_t(1, 3, 32, 10000.0)
+    assert lib.fa_rope_apply(_lib.FA_DTYPE_BF16, 1, 4, 1, 128, None, None, C.byref(r), 0,
+                             None) == _lib.FA_ERR_UNSUPPORTED
+
+
+def test_workspace_sizes():
+    from foundry_trainer_b200 import _lib
+    lib = _lib.load()
+    B, S, H, D = 1, 4608, 24, 128
+    assert lib.fa_fwd_workspace_bytes(_lib.FA_DTYPE_BF16, B, S, H, D, None) == 0
+    r = _lib.fa_rope_t(1, 4, 32, 10000.0)
+    assert lib.fa_fwd_workspace_bytes(_lib.FA_DTYPE_BF16, B, S, H, D, C.byref(r)) >= 2 * B * S * H * D * 2
+    ws = lib.fa_bwd_workspace_bytes(_lib.FA_DTYPE_BF16, B, S, H, D, None, 0)
+    assert ws >= B * S * H * D * 4 + 2 * B * H * S * 4
+
+
+def test_loading_missing_library_fails_loudly(tmp_path, monkeypatch):
+    from foundry_trainer_b200 import _lib
+    monkeypatch.setattr(_lib, "_lib", None)
+    monkeypatch.setattr(_lib, "LIB_PATH", tmp_path / "nope.so")
+    with pytest.raises(_lib.FaError):
+        _lib.load()

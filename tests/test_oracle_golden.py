@@ -1,0 +1,83 @@
+"""Pins the CPU oracle to the reference's own golden vectors (no GPU).
+
+The reference validated its Candle op against these PyTorch-generated
+fixtures (src/bin/attn_backward.rs:203-233, tools/fixtures/PROVENANCE.md);
+the oracle must reproduce them before it may judge the B200 kernels.
+"""
+import numpy as np
+import pytest
+
+from oracle import attn_oracle as orc
+
+
+def _load(golden_dir, name):
+    return dict(np.load(golden_dir / name))
+
+
+@pytest.mark.parametrize("blk", ["double", "single"])
+def test_oracle_matches_fp32_fixture(golden_dir, blk):
+    g = _load(golden_dir, "attn_fixture_fp32.npz")
+    q, k, v, dout = (g[f"{blk}_{n}"] for n in ("q", "k", "v", "dout"))
+    o = orc.attn_fwd(q, k, v, "f32")
+    dq, dk, dv = orc.attn_bwd(q, k, v, dout, "f32")
+    for name, ours, ref in (("o", o, g[f"{blk}_attn"]), ("dq", dq, g[f"{blk}_dq"]),
+                            ("dk", dk, g[f"{blk}_dk"]), ("dv", dv, g[f"{blk}_dv"])):
+        assert orc.max_rel(ours, ref) <= 2e-6, name
+
+
+@pytest.mark.parametrize("blk", ["double", "single"])
+def test_oracle_matches_bf16_fixture(golden_dir, blk):
+    g = _load(golden_dir, "attn_fixture_bf16.npz")
+    q, k, v, dout = (g[f"{blk}_{n}"] for n in ("q", "k", "v", "dout"))
+    o = orc.attn_fwd(q, k, v, "bf16")
+    dq, dk, dv = orc.attn_bwd(q, k, v, dout, "bf16")
+    for name, ours, ref in (("o", o, g[f"{blk}_attn"]), ("dq", dq, g[f"{blk}_dq"]),
+                            ("dk", dk, g[f"{blk}_dk"]), ("dv", dv, g[f"{blk}_dv"])):
+        # bit-identical except where fp32 accumulation order moves a bf16 rounding
+        assert orc.max_rel(ours, ref) <= 1e-4, name
+        cos, rel = orc.compare(ours, ref)
+        assert cos >= 0.9999999 and rel <= 1e-5, name
+
+
+@pytest.mark.parametrize("tag,tol", [("fp32", 2e-6), ("bf16", 1e-4)])
+def test_oracle_rope_matches_fixture(golden_dir, tag, tol):
+    g = _load(golden_dir, f"rope_fixture_{tag}.npz")
+    dt = "f32" if tag == "fp32" else "bf16"
+    cases = sorted({k.rsplit("_", 1)[0] for k in g})
+    assert len(cases) == 6
+    for c in cases:
+        cos, sin = orc.rope_tables(g[f"{c}_pos"], dt)
+        post = orc.apply_rope(g[f"{c}_pre"], cos, sin, dt)
+        assert orc.max_rel(post, g[f"{c}_post"]) <= tol, c
+
+
+def test_oracle_rope_inside_op_fixture(golden_dir):
+    g = _load(golden_dir, "attn_rope_fixture_fp32.npz")
+    o, lse, dq, dk, dv = orc.attn_fwd_bwd_bshd(g["q"][None], g["k"][None], g["v"][None],
+                                               g["dout"][None], "f32", rope_pos=g["pos"])
+    for name, ours, ref in (("o", o[0], g["o"]), ("dq", dq[0], g["dq"]), ("dk", dk[0], g["dk"]),
+                            ("dv", dv[0], g["dv"])):
+        assert orc.max_rel(ours, ref) <= 1e-5, name
+
+
+def test_oracle_lse_is_logsumexp():
+    rng = np.random.default_rng(0)
+    q, k, v = (rng.standard_normal((40, 3, 128)).astype(np.float32) for _ in range(3))
+    _, lse = orc.attn_fwd(q, k, v, "f32", return_lse=True)
+    s = np.einsum("shd,thd->hst", q.astype(np.float64), k.astype(np.float64)) / np.sqrt(128)
+    ref = np.log(np.exp(s).sum(-1))
+    assert np.abs(lse - ref).max() < 1e-4
+
+
+def test_bf16_round_ties_to_even():
+    x = np.array([1.0, 1.00390625, 1.01171875, -2.5, 3.0e38], dtype=np.float32)
+    r = orc.bf16_round(x)
+    # 1 + 2^-8 is a tie between 1 and 1 + 2^-7 -> even (1.0); 1 + 3*2^-8 -> 1 + 2^-6
+    assert r[0] == 1.0 and r[1] == 1.0 and r[2] == np.float32(1.015625)
+    assert r[3] == -2.5
+
+
+def test_max_rel_definition():
+    ref = np.array([1.0, -4.0, 2.0])
+    ours = np.array([1.1, -4.0, 2.0])
+    assert abs(orc.max_rel(ours, ref) - 0.1 / 4.0) < 1e-12
