@@ -16,7 +16,7 @@ def test_fp32_fixture_replay(golden_dir):
     for blk in ("double", "single"):
         q, k, v, dout = (torch.from_numpy(g[f"{blk}_{n}"]).cuda() for n in ("q", "k", "v", "dout"))
         o, lse, dq, dk, dv = run_op(q, k, v, dout)
-        assert_close({"o": o[0], "dq": dq[0], "dk": dk[0], "dv": dv[0]},
+        assert_close({"o": o, "dq": dq, "dk": dk, "dv": dv},
                      {"o": g[f"{blk}_attn"], "dq": g[f"{blk}_dq"], "dk": g[f"{blk}_dk"],
                       "dv": g[f"{blk}_dv"]}, 1e-4, blk)
 
@@ -41,7 +41,7 @@ def test_fp32_rope_inside_op_fixture(golden_dir):
     q, k, v, dout = (torch.from_numpy(g[n]).cuda() for n in ("q", "k", "v", "dout"))
     rope = ops.Rope(torch.from_numpy(g["pos"]).cuda())
     o, lse, dq, dk, dv = run_op(q, k, v, dout, rope=rope)
-    assert_close({"o": o[0], "dq": dq[0], "dk": dk[0], "dv": dv[0]},
+    assert_close({"o": o, "dq": dq, "dk": dk, "dv": dv},
                  {"o": g["o"], "dq": g["dq"], "dk": g["dk"], "dv": g["dv"]}, 1e-4, "rope fixture")
 
 
