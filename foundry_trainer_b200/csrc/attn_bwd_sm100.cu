@@ -430,7 +430,8 @@ int launch_attn_bwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
                          const float* delta_pad, float* dq_acc,
                          const fa_tensor_t* dk, const fa_tensor_t* dv,
                          float* dk_acc, float* dv_acc, float scale,
-                         const fa_rope_t* rope, cudaStream_t stream) {
+                         const fa_rope_t* rope, const float2* rope_table,
+                         cudaStream_t stream) {
   CUtensorMap tq, tk, tv, tdo;
   int rc = make_tmap_bshd(&tq, q, sh.B, sh.S, sh.H, sh.D, 128);
   if (!rc) rc = make_tmap_bshd(&tk, k, sh.B, kv_len, sh.H, sh.D, 128);
@@ -460,6 +461,7 @@ int launch_attn_bwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
   p.dk_acc = dk_acc;
   p.dv_acc = dv_acc;
   p.rope = make_rope_args(rope);
+  p.rope.table = rope_table;
   rc = ensure_smem_attr((const void*)bwd::attn_bwd_kernel, bwd::kSmemBytes,
                         kKernelBwdBf16);
   if (rc) return rc;

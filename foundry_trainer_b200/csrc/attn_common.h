@@ -48,7 +48,8 @@ int launch_attn_bwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
                          const float* delta_pad, float* dq_acc,
                          const fa_tensor_t* dk, const fa_tensor_t* dv,
                          float* dk_acc, float* dv_acc, float scale,
-                         const fa_rope_t* rope, cudaStream_t stream);
+                         const fa_rope_t* rope, const float2* rope_table,
+                         cudaStream_t stream);
 
 // fp32 SIMT kernels (exact path)
 int launch_attn_fwd_f32(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
@@ -68,12 +69,20 @@ int launch_attn_bwd_f32(const AttnShape& sh, const fa_tensor_t* q,
 int launch_bwd_delta(int dtype, const AttnShape& sh, const fa_tensor_t* o,
                      const fa_tensor_t* d_o, const float* lse, float* delta,
                      float* lse2, int s_pad, cudaStream_t stream);
+// (cos, sin) table for tokens [0, S) (+pos_offset), S * n_axes*axis_dim/2 float2
+int launch_rope_table(int dtype, int S, const fa_rope_t* rope, int pos_offset,
+                      float2* table, cudaStream_t stream);
+// table may be nullptr (cos/sin evaluated per element)
 int launch_rope(int dtype, const AttnShape& sh, const fa_tensor_t* x,
                 const fa_tensor_t* y, const fa_rope_t* rope, int inverse,
-                int pos_offset, cudaStream_t stream);
+                int pos_offset, cudaStream_t stream, const float2* table = nullptr);
+int launch_rope_pair(int dtype, const AttnShape& sh, const fa_tensor_t* x0,
+                     const fa_tensor_t* y0, const fa_tensor_t* x1,
+                     const fa_tensor_t* y1, const fa_rope_t* rope, int inverse,
+                     int pos_offset, cudaStream_t stream, const float2* table);
 int launch_cast_f32(int dtype, const AttnShape& sh, const float* x,
                     const fa_tensor_t* y, float alpha, const fa_rope_t* rope,
-                    int pos_offset, cudaStream_t stream);
+                    int pos_offset, cudaStream_t stream, const float2* table = nullptr);
 int launch_lse_merge(int dtype, const AttnShape& sh, float* o_acc,
                      float* lse_acc, const fa_tensor_t* o_blk,
                      const float* lse_blk, int first, cudaStream_t stream);

@@ -148,6 +148,12 @@ static int check_rope(const fa_rope_t* rope, int D) {
 
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
+// bytes of the per-call (cos, sin) table: S tokens x n_axes*axis_dim/2 float2
+static size_t rope_table_bytes(int S, const fa_rope_t* rope) {
+  if (rope == nullptr) return 0;
+  return align256((size_t)S * (size_t)(rope->n_axes * (rope->axis_dim / 2)) * sizeof(float2));
+}
+
 static fa_tensor_t contiguous_view(void* p, int S, int H, int D) {
   fa_tensor_t t;
   t.data = p;
@@ -240,7 +246,7 @@ size_t fa_fwd_workspace_bytes(int dtype, int B, int S, int H, int D,
                               const fa_rope_t* rope) {
   if (rope == nullptr) return 0;
   const size_t es = dtype == FA_DTYPE_BF16 ? 2 : 4;
-  return 2 * align256((size_t)B * S * H * D * es);
+  return rope_table_bytes(S, rope) + 2 * align256((size_t)B * S * H * D * es);
 }
 
 int fa_fwd(int dtype, int B, int S, int H, int D, const fa_tensor_t* q,
@@ -265,10 +271,13 @@ int fa_fwd(int dtype, int B, int S, int H, int D, const fa_tensor_t* q,
     const size_t need = fa_fwd_workspace_bytes(dtype, B, S, H, D, rope);
     if (workspace == nullptr || workspace_bytes < need) return FA_ERR_WORKSPACE;
     uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+    float2* table = reinterpret_cast<float2*>(ws);
+    ws += rope_table_bytes(S, rope);
+    const size_t tb = align256((size_t)B * S * H * D * es);
     qr = contiguous_view(ws, S, H, D);
-    kr = contiguous_view(ws + need / 2, S, H, D);
-    FA_TRY(launch_rope(dtype, sh, q, &qr, rope, 0, 0, st));
-    FA_TRY(launch_rope(dtype, sh, k, &kr, rope, 0, 0, st));
+    kr = contiguous_view(ws + tb, S, H, D);
+    FA_TRY(launch_rope_table(dtype, S, rope, 0, table, st));
+    FA_TRY(launch_rope_pair(dtype, sh, q, &qr, k, &kr, rope, 0, 0, st, table));
   }
   cudaEvent_t stop = timer_begin(FA_TIMER_FWD, st);
   const int rc = bf ? launch_attn_fwd_bf16(sh, &qr, &kr, v, o, lse, scale, st)
@@ -285,13 +294,13 @@ size_t fa_bwd_workspace_bytes(int dtype, int B, int S, int H, int D,
   const size_t n = (size_t)B * S * H * D;
   if (dtype == FA_DTYPE_BF16) {
     const size_t s_pad = (size_t)((S + 127) / 128) * 128;
-    size_t total = 0;
+    size_t total = rope_table_bytes(S, rope);
     if (rope) total += 2 * align256(n * 2);
     total += 2 * align256((size_t)B * H * s_pad * 4);
     total += align256(n * 4);
     return total;
   }
-  size_t total = 0;
+  size_t total = rope_table_bytes(S, rope);
   if (rope) total += 4 * align256(n * 4);
   total += align256((size_t)B * H * S * 4);
   return total;
@@ -320,14 +329,19 @@ int fa_bwd(int dtype, int B, int S, int H, int D, const fa_tensor_t* q,
   uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
   const size_t n = (size_t)B * S * H * D;
   fa_tensor_t qr = *q, kr = *k;
+  float2* table = nullptr;
+  if (rope) {
+    table = reinterpret_cast<float2*>(ws);
+    ws += rope_table_bytes(S, rope);
+    FA_TRY(launch_rope_table(dtype, S, rope, 0, table, st));
+  }
   if (bf) {
     if (rope) {
       qr = contiguous_view(ws, S, H, D);
       ws += align256(n * 2);
       kr = contiguous_view(ws, S, H, D);
       ws += align256(n * 2);
-      FA_TRY(launch_rope(dtype, sh, q, &qr, rope, 0, 0, st));
-      FA_TRY(launch_rope(dtype, sh, k, &kr, rope, 0, 0, st));
+      FA_TRY(launch_rope_pair(dtype, sh, q, &qr, k, &kr, rope, 0, 0, st, table));
     }
     const int s_pad = ((S + 127) / 128) * 128;
     float* lse2 = reinterpret_cast<float*>(ws);
@@ -340,10 +354,10 @@ int fa_bwd(int dtype, int B, int S, int H, int D, const fa_tensor_t* q,
     cudaEvent_t stop = timer_begin(FA_TIMER_BWD, st);
     const int rc = launch_attn_bwd_bf16(sh, S, &qr, &kr, v, d_o, lse2, delta,
                                         dq_acc, dk, dv, nullptr, nullptr, scale,
-                                        rope, st);
+                                        rope, table, st);
     timer_end(stop, st);
     FA_TRY(rc);
-    return launch_cast_f32(dtype, sh, dq_acc, dq, scale, rope, 0, st);
+    return launch_cast_f32(dtype, sh, dq_acc, dq, scale, rope, 0, st, table);
   }
   // fp32 path
   fa_tensor_t dqr = *dq, dkr = *dk;
@@ -356,8 +370,7 @@ int fa_bwd(int dtype, int B, int S, int H, int D, const fa_tensor_t* q,
     ws += align256(n * 4);
     dkr = contiguous_view(ws, S, H, D);
     ws += align256(n * 4);
-    FA_TRY(launch_rope(dtype, sh, q, &qr, rope, 0, 0, st));
-    FA_TRY(launch_rope(dtype, sh, k, &kr, rope, 0, 0, st));
+    FA_TRY(launch_rope_pair(dtype, sh, q, &qr, k, &kr, rope, 0, 0, st, table));
   }
   float* delta = reinterpret_cast<float*>(ws);
   FA_TRY(launch_bwd_delta(dtype, sh, o, d_o, lse, delta, nullptr, S, st));
@@ -366,10 +379,7 @@ int fa_bwd(int dtype, int B, int S, int H, int D, const fa_tensor_t* q,
                                      &dkr, dv, scale, st);
   timer_end(stop, st);
   FA_TRY(rc);
-  if (rope) {
-    FA_TRY(launch_rope(dtype, sh, &dqr, dq, rope, 1, 0, st));
-    FA_TRY(launch_rope(dtype, sh, &dkr, dk, rope, 1, 0, st));
-  }
+  if (rope) FA_TRY(launch_rope_pair(dtype, sh, &dqr, dq, &dkr, dk, rope, 1, 0, st, table));
   return FA_OK;
 }
 

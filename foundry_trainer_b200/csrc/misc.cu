@@ -71,12 +71,15 @@ __global__ void delta_kernel(TView o, TView d_o, const float* lse, float* delta,
 }
 
 // One warp per row: y = rot(x) (or the inverse), fp32 math, axis_dim == 32.
+// blockIdx.y selects one of two (x, y) pairs so q and k rotate in one launch.
 template <typename Tin, typename Tout>
-__global__ void rope_warp_kernel(TView x, TOut y, RopeArgs r, int S, int H,
-                                 int B, float alpha, int inverse) {
+__global__ void rope_warp_kernel(TView x0, TOut y0, TView x1, TOut y1, RopeArgs r,
+                                 int S, int H, int B, float alpha, int inverse) {
   const int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= (int64_t)B * S * H) return;
+  const TView& x = blockIdx.y == 0 ? x0 : x1;
+  const TOut& y = blockIdx.y == 0 ? y0 : y1;
   const int h = (int)(row % H);
   const int64_t bs = row / H;
   const int s = (int)(bs % S), b = (int)(bs / S);
@@ -86,28 +89,33 @@ __global__ void rope_warp_kernel(TView x, TOut y, RopeArgs r, int S, int H,
 #pragma unroll
   for (int a = 0; a < 4; ++a) v[a] = ld_elem<Tin>(px + lane + 32 * a) * alpha;
   if (r.pos != nullptr) {
-    const float* pos = r.pos + (int64_t)(s + r.pos_offset) * r.n_axes;
     const int j = lane & 15;
     const bool first = lane < 16;
+    // forward: y1 = x1 c - x2 s, y2 = x2 c + x1 s; inverse: the transpose
+    const float sgn = (first != (inverse != 0)) ? -1.f : 1.f;
 #pragma unroll
     for (int a = 0; a < 4; ++a) {
       const float other = __shfl_xor_sync(0xffffffffu, v[a], 16);
       if (a < r.n_axes) {
-        const float f = __fmul_rn(pos[a], r.inv_freq[a * 16 + j]);
-        float sn, cs;
-        sincosf(f, &sn, &cs);
-        if (r.round_bf16) {
-          cs = round_bf16_f(cs);
-          sn = round_bf16_f(sn);
-        }
-        // forward: y1 = x1 c - x2 s, y2 = x2 c + x1 s; inverse: transpose
-        const float sgn = (first != (inverse != 0)) ? -1.f : 1.f;
-        v[a] = __fadd_rn(__fmul_rn(v[a], cs), __fmul_rn(sgn * other, sn));
+        const float2 cs = rope_cs(r, s, a * 16 + j);
+        v[a] = __fadd_rn(__fmul_rn(v[a], cs.x), __fmul_rn(sgn * other, cs.y));
       }
     }
   }
 #pragma unroll
   for (int a = 0; a < 4; ++a) st_elem<Tout>(py + lane + 32 * a, v[a]);
+}
+
+// (cos, sin) per (token, frequency), rounded to the compute dtype: evaluated
+// once per call and reused by every head, batch and kernel of that call.
+__global__ void rope_table_kernel(RopeArgs r, int S, float2* table) {
+  const int nf = r.n_axes * (r.axis_dim >> 1);
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)S * nf) return;
+  const int t = (int)(i / nf), f = (int)(i % nf);
+  RopeArgs direct = r;
+  direct.table = nullptr;
+  table[(int64_t)(t + r.pos_offset) * nf + f] = rope_cs(direct, t, f);
 }
 
 // Generic thread-per-row rotation for other axis layouts.
@@ -183,20 +191,31 @@ int launch_bwd_delta(int dtype, const AttnShape& sh, const fa_tensor_t* o,
 static int launch_rope_generic(int dtype_in, int dtype_out, const AttnShape& sh,
                                const misc::TView& x, const misc::TOut& y,
                                const RopeArgs& r, float alpha, int inverse,
-                               cudaStream_t stream) {
+                               cudaStream_t stream,
+                               const misc::TView* xb = nullptr,
+                               const misc::TOut* yb = nullptr) {
+  const unsigned npairs = xb != nullptr ? 2u : 1u;
+  const misc::TView x2 = xb != nullptr ? *xb : x;
+  const misc::TOut y2 = yb != nullptr ? *yb : y;
   const int64_t rows = (int64_t)sh.B * sh.S * sh.H;
   const bool warp_path = (r.pos == nullptr) || (r.axis_dim == 32 && r.n_axes <= 4);
   if (warp_path) {
     const dim3 grid((unsigned)((rows + misc::kWarps - 1) / misc::kWarps));
     const int nt = 32 * misc::kWarps;
-#define FA_ROPE_W(TI, TO) \
-  misc::rope_warp_kernel<TI, TO><<<grid, nt, 0, stream>>>(x, y, r, sh.S, sh.H, sh.B, alpha, inverse)
+#define FA_ROPE_W(TI, TO)                                                       \
+  misc::rope_warp_kernel<TI, TO><<<dim3(grid.x, npairs), nt, 0, stream>>>(       \
+      x, y, x2, y2, r, sh.S, sh.H, sh.B, alpha, inverse)
     if (dtype_in == FA_DTYPE_BF16 && dtype_out == FA_DTYPE_BF16) FA_ROPE_W(__nv_bfloat16, __nv_bfloat16);
     else if (dtype_in == FA_DTYPE_F32 && dtype_out == FA_DTYPE_BF16) FA_ROPE_W(float, __nv_bfloat16);
     else if (dtype_in == FA_DTYPE_F32 && dtype_out == FA_DTYPE_F32) FA_ROPE_W(float, float);
     else FA_ROPE_W(__nv_bfloat16, float);
 #undef FA_ROPE_W
   } else {
+    if (npairs == 2) {
+      const int rc = launch_rope_generic(dtype_in, dtype_out, sh, x2, y2, r, alpha,
+                                         inverse, stream);
+      if (rc != FA_OK) return rc;
+    }
     const dim3 grid((unsigned)((rows + 127) / 128));
 #define FA_ROPE_R(TI, TO) \
   misc::rope_row_kernel<TI, TO><<<grid, 128, 0, stream>>>(x, y, r, sh.S, sh.H, sh.B, alpha, inverse)
@@ -209,18 +228,40 @@ static int launch_rope_generic(int dtype_in, int dtype_out, const AttnShape& sh,
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
+int launch_rope_table(int dtype, int S, const fa_rope_t* rope, int pos_offset,
+                      float2* table, cudaStream_t stream) {
+  const RopeArgs r = make_rope_args(rope, dtype == FA_DTYPE_BF16 ? 1 : 0, pos_offset);
+  const int64_t n = (int64_t)S * r.n_axes * (r.axis_dim / 2);
+  misc::rope_table_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(r, S, table);
+  return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+}
+
 int launch_rope(int dtype, const AttnShape& sh, const fa_tensor_t* x,
                 const fa_tensor_t* y, const fa_rope_t* rope, int inverse,
-                int pos_offset, cudaStream_t stream) {
-  const RopeArgs r = make_rope_args(rope, dtype == FA_DTYPE_BF16 ? 1 : 0, pos_offset);
+                int pos_offset, cudaStream_t stream, const float2* table) {
+  RopeArgs r = make_rope_args(rope, dtype == FA_DTYPE_BF16 ? 1 : 0, pos_offset);
+  r.table = table;
   return launch_rope_generic(dtype, dtype, sh, misc::tview(x), misc::tout(y), r,
                              1.f, inverse, stream);
 }
 
+int launch_rope_pair(int dtype, const AttnShape& sh, const fa_tensor_t* x0,
+                     const fa_tensor_t* y0, const fa_tensor_t* x1,
+                     const fa_tensor_t* y1, const fa_rope_t* rope, int inverse,
+                     int pos_offset, cudaStream_t stream, const float2* table) {
+  RopeArgs r = make_rope_args(rope, dtype == FA_DTYPE_BF16 ? 1 : 0, pos_offset);
+  r.table = table;
+  const misc::TView xb = misc::tview(x1);
+  const misc::TOut yb = misc::tout(y1);
+  return launch_rope_generic(dtype, dtype, sh, misc::tview(x0), misc::tout(y0), r,
+                             1.f, inverse, stream, &xb, &yb);
+}
+
 int launch_cast_f32(int dtype, const AttnShape& sh, const float* x,
                     const fa_tensor_t* y, float alpha, const fa_rope_t* rope,
-                    int pos_offset, cudaStream_t stream) {
-  const RopeArgs r = make_rope_args(rope, dtype == FA_DTYPE_BF16 ? 1 : 0, pos_offset);
+                    int pos_offset, cudaStream_t stream, const float2* table) {
+  RopeArgs r = make_rope_args(rope, dtype == FA_DTYPE_BF16 ? 1 : 0, pos_offset);
+  r.table = table;
   const int64_t D = sh.D;
   misc::TView xv{x, (int64_t)sh.S * sh.H * D, (int64_t)sh.H * D, D};
   return launch_rope_generic(FA_DTYPE_F32, dtype, sh, xv, misc::tout(y), r,

@@ -25,6 +25,10 @@ struct RopeArgs {
   int axis_dim;
   int round_bf16;    // 1: round cos/sin to bf16 (compute dtype bf16)
   int pos_offset;    // token index offset into pos (sequence shards)
+  // Optional precomputed (cos, sin) per (token, frequency), tokens indexed
+  // like pos (pos_offset applies), n_axes * axis_dim / 2 entries per token,
+  // already rounded to the compute dtype. nullptr: evaluate from pos.
+  const float2* table;
   float inv_freq[kMaxRopeFreqs];  // theta^(-2j/dim_a), j < dim_a/2
 };
 
@@ -37,25 +41,34 @@ __device__ __forceinline__ float round_bf16_f(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));
 }
 
+// (cos, sin) of frequency f (axis f / half, index f % half) for `token`.
+__device__ __forceinline__ float2 rope_cs(const RopeArgs& r, int token, int f) {
+  const int t = token + r.pos_offset;
+  const int nf = r.n_axes * (r.axis_dim >> 1);
+  if (r.table != nullptr) return r.table[(int64_t)t * nf + f];
+  const int half = r.axis_dim >> 1;
+  const float a = __fmul_rn(r.pos[(int64_t)t * r.n_axes + f / half], r.inv_freq[f]);
+  float sn, cs;
+  sincosf(a, &sn, &cs);
+  if (r.round_bf16) {
+    cs = round_bf16_f(cs);
+    sn = round_bf16_f(sn);
+  }
+  return make_float2(cs, sn);
+}
+
 // Rotates (inverse == false) or un-rotates one 128-wide row in place.
 __device__ __forceinline__ void rope_rotate_row128(const RopeArgs& r,
                                                    int token, float* v,
                                                    bool inverse) {
   const int half = r.axis_dim >> 1;
-  const float* pos = r.pos + (int64_t)(token + r.pos_offset) * r.n_axes;
 #pragma unroll 1
   for (int a = 0; a < r.n_axes; ++a) {
-    const float pa = pos[a];
     float* seg = v + a * r.axis_dim;
 #pragma unroll 4
     for (int j = 0; j < half; ++j) {
-      const float f = __fmul_rn(pa, r.inv_freq[a * half + j]);
-      float s, c;
-      sincosf(f, &s, &c);
-      if (r.round_bf16) {
-        c = round_bf16_f(c);
-        s = round_bf16_f(s);
-      }
+      const float2 cs = rope_cs(r, token, a * half + j);
+      const float c = cs.x, s = cs.y;
       const float x1 = seg[j];
       const float x2 = seg[j + half];
       if (!inverse) {
