@@ -15,13 +15,16 @@
 //   warp 8      TMA producer: K, V once; Q_i, dO_i, LSE_i, Delta_i per step
 //   warp 9      tcgen05 MMA issuer, TMEM owner
 //   warps 0-3   softmax backward, one key row per thread; dV epilogue
-//   warps 4-7   dQ drain (fp32 vector reductions into dq_acc); dK epilogue
+//   warps 4-7   dQ drain: TMEM -> swizzled shared tile -> TMA bulk reduce-add
+//               (fp32) into dq_acc; dK epilogue
 // TMEM (512 columns):
 //   A [0,128)    S^T_i, then P^T_i (bf16, cols 0-63) | dS^T_i (bf16, 64-127)
 //   B [128,256)  dP^T_i, then dQ_i (fp32, query rows)
 //   dV [256,384) dK [384,512)   accumulators over all Q tiles
 // Every MMA that overwrites columns another MMA reads waits for that MMA's
-// commit first; dQ_i is drained while S^T_{i+1} runs.
+// commit first; dQ_i is drained while S^T_{i+1} runs. The dQ drain stages
+// through the dS^T shared tile (free once the dQ MMA has read it) and hands it
+// back to the softmax warps (DSFREE) when the bulk reduce has read it.
 #include "attn_common.h"
 #include "rope.cuh"
 #include "sm100_ptx.cuh"
@@ -55,6 +58,7 @@ constexpr int B_DQFULL = 7;
 constexpr int B_DQFREE = 8;
 constexpr int B_DVK = 9;
 constexpr int B_FINAL = 10;
+constexpr int B_DSFREE = 11;
 
 constexpr uint32_t kColA = 0;
 constexpr uint32_t kColB = 128;
@@ -78,12 +82,6 @@ struct Params {
   RopeArgs rope;            // rope.pos == nullptr: no rotation
 };
 
-__device__ __forceinline__ float fast_exp2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
 __device__ __forceinline__ void bulk_load(void* dst, const void* src,
                                           uint32_t bytes, uint64_t* bar) {
   asm volatile(
@@ -91,13 +89,6 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src,
       "[%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
-}
-
-__device__ __forceinline__ void red_add_v4(float* addr, float a, float b,
-                                           float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr),
-               "f"(a), "f"(b), "f"(c), "f"(d)
-               : "memory");
 }
 
 // Writes one 128-value fp32 row held in registers to a dK/dV destination.
@@ -139,7 +130,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                 const __grid_constant__ CUtensorMap tm_k,
                 const __grid_constant__ CUtensorMap tm_v,
-                const __grid_constant__ CUtensorMap tm_do, Params p) {
+                const __grid_constant__ CUtensorMap tm_do,
+                const __grid_constant__ CUtensorMap tm_dq, Params p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc);
@@ -170,6 +162,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
     mbar_init(&bars[B_DQFREE], 128);
     mbar_init(&bars[B_DVK], 1);
     mbar_init(&bars[B_FINAL], 1);
+    mbar_init(&bars[B_DSFREE], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -294,40 +287,47 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
       ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_QFULL + st], n & 1));
       if (!ok) break;
       tc_fence_after();
-      const float* lse2 = reinterpret_cast<const float*>(smem + kOffLse + st * 512);
-      const float* dlt = reinterpret_cast<const float*>(smem + kOffDelta + st * 512);
-      uint32_t pr[128];
-      tmem_ld32(t_a + 0, pr);
-      tmem_ld32(t_a + 32, pr + 32);
-      tmem_ld32(t_a + 64, pr + 64);
-      tmem_ld32(t_a + 96, pr + 96);
-      tmem_wait_ld();
-      float* pv = reinterpret_cast<float*>(pr);
-#pragma unroll
-      for (int c = 0; c < 128; ++c) pv[c] = fast_exp2(fmaf(pv[c], sl2, -lse2[c]));
-#pragma unroll
-      for (int cb = 0; cb < 4; ++cb) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int u = 0; u < 16; ++u)
-          pk[u] = pack_bf16(pv[cb * 32 + 2 * u], pv[cb * 32 + 2 * u + 1]);
-        tmem_st16(t_a + cb * 16, pk);
+      const float4* lse4 = reinterpret_cast<const float4*>(smem + kOffLse + st * 512);
+      const float4* dlt4 = reinterpret_cast<const float4*>(smem + kOffDelta + st * 512);
+      // S^T columns 64-127 are read first: dS^T of query chunks 0-3 is
+      // written over them (columns 64-127), P^T of chunk c over S^T columns
+      // 16c..16c+15, which chunk c (or an earlier one) has already read.
+      uint32_t s_hi[64];
+      tmem_ld32(t_a + 64, s_hi);
+      tmem_ld32(t_a + 96, s_hi + 32);
+      // the drain of dQ_{i-1} must have released the shared dS^T tile
+      if (i > 0) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_DSFREE], (i - 1) & 1));
+        if (!ok) break;
       }
 #pragma unroll
       for (int cb = 0; cb < 4; ++cb) {
-        uint32_t dr[32];
+        uint32_t s_lo[32], dr[32];
+        if (cb < 2) tmem_ld32(t_a + cb * 32, s_lo);
         tmem_ld32(t_b + cb * 32, dr);
         tmem_wait_ld();
-        uint32_t pk[16];
+        const uint32_t* sr = cb < 2 ? s_lo : s_hi + (cb - 2) * 32;
+        uint32_t pk[16], dk[16];
 #pragma unroll
-        for (int u = 0; u < 16; ++u) {
-          const int c0 = cb * 32 + 2 * u;
-          const float d0 = pv[c0] * (__uint_as_float(dr[2 * u]) - dlt[c0]);
-          const float d1 =
-              pv[c0 + 1] * (__uint_as_float(dr[2 * u + 1]) - dlt[c0 + 1]);
-          pk[u] = pack_bf16(d0, d1);
+        for (int u = 0; u < 8; ++u) {
+          const float4 l = lse4[cb * 8 + u];
+          const float4 dl = dlt4[cb * 8 + u];
+          const int c = 4 * u;
+          const float p0 = exp2_mixed<0>(fmaf(__uint_as_float(sr[c + 0]), sl2, -l.x));
+          const float p1 = exp2_mixed<1>(fmaf(__uint_as_float(sr[c + 1]), sl2, -l.y));
+          const float p2 = exp2_mixed<0>(fmaf(__uint_as_float(sr[c + 2]), sl2, -l.z));
+          const float p3 = exp2_mixed<1>(fmaf(__uint_as_float(sr[c + 3]), sl2, -l.w));
+          pk[2 * u] = pack_bf16_alu(p0, p1);
+          pk[2 * u + 1] = pack_bf16_alu(p2, p3);
+          const float d0 = p0 * (__uint_as_float(dr[c + 0]) - dl.x);
+          const float d1 = p1 * (__uint_as_float(dr[c + 1]) - dl.y);
+          const float d2 = p2 * (__uint_as_float(dr[c + 2]) - dl.z);
+          const float d3 = p3 * (__uint_as_float(dr[c + 3]) - dl.w);
+          dk[2 * u] = pack_bf16_alu(d0, d1);
+          dk[2 * u + 1] = pack_bf16_alu(d2, d3);
         }
-        tmem_st16(t_a + 64 + cb * 16, pk);
+        tmem_st16(t_a + cb * 16, pk);
+        tmem_st16(t_a + 64 + cb * 16, dk);
         // dS^T row -> shared memory: queries [32cb, 32cb+32) are 16-byte
         // chunks 4*(cb&1) .. +3 of swizzle block cb>>1.
         uint8_t* blk = ds_row + (cb >> 1) * kBlkBytes;
@@ -335,7 +335,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
         for (int u = 0; u < 4; ++u) {
           const uint32_t off = sw128_offset(key_in_tile, (cb & 1) * 4 + u);
           *reinterpret_cast<uint4*>(blk + off) =
-              make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+              make_uint4(dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
         }
       }
       tmem_wait_st();
@@ -365,11 +365,14 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
     const int row_in_tile = sub * 32 + lane;
     const uint32_t lane_off = (uint32_t)(sub * 32) << 16;
     const uint32_t t_b = tmem + lane_off + kColB;
+    const bool leader = (warp == 4 && lane == 0);
+    uint8_t* stage = smem + kOffDS;  // two 16 KB boxes of 32 fp32 columns
     bool ok = true;
     for (int i = 0; i < nq; ++i) {
-      if (__any_sync(0xffffffffu, *abort_flag != 0)) { ok = false; break; }
-      ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_DQFULL], i & 1));
-      if (!ok) break;
+      // leave together: the passes below use a named barrier over warps 4-7
+      bool stop = *abort_flag != 0;
+      if (!stop) stop = !mbar_wait(&bars[B_DQFULL], i & 1);
+      if (named_bar_any(2, 128, stop)) { ok = false; break; }
       tc_fence_after();
       uint32_t r[128];
       tmem_ld32(t_b + 0, r);
@@ -379,16 +382,39 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(&bars[B_DQFREE]);
-      const int q = i * kRows + row_in_tile;
-      if (q < p.S) {
-        float* dst = p.dq_acc + (((int64_t)b * p.S + q) * p.H + h) * 128;
-        const float* v = reinterpret_cast<const float*>(r);
+      // two passes of 64 columns through the 32 KB dS^T tile (the dQ MMA,
+      // its only reader, has completed: DQFULL)
 #pragma unroll
-        for (int c = 0; c < 32; ++c)
-          red_add_v4(dst + 4 * c, v[4 * c], v[4 * c + 1], v[4 * c + 2],
-                     v[4 * c + 3]);
+      for (int pass = 0; pass < 2; ++pass) {
+        if (pass == 1) {
+          // the first pass's bulk reduce must have read the tile
+          if (leader) bulk_wait_group_read0();
+          named_bar_sync(2, 128);
+        }
+#pragma unroll
+        for (int bx = 0; bx < 2; ++bx) {
+          uint8_t* box = stage + bx * kBlkBytes;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const int col = pass * 64 + bx * 32 + c * 4;
+            *reinterpret_cast<uint4*>(box + sw128_offset(row_in_tile, c)) =
+                make_uint4(r[col], r[col + 1], r[col + 2], r[col + 3]);
+          }
+        }
+        fence_proxy_async_smem();
+        named_bar_sync(2, 128);
+        if (leader) {
+          tma_reduce_add_4d(&tm_dq, stage, pass * 64, i * kRows, h, b);
+          tma_reduce_add_4d(&tm_dq, stage + kBlkBytes, pass * 64 + 32, i * kRows, h, b);
+          bulk_commit_group();
+        }
+      }
+      if (leader) {
+        bulk_wait_group_read0();
+        mbar_arrive(&bars[B_DSFREE]);
       }
     }
+    if (leader) bulk_wait_group0();  // reductions complete before exit
     // dK epilogue: scale, inverse rotation (when the op owns the RoPE)
     if (ok && __all_sync(0xffffffffu, mbar_wait(&bars[B_FINAL], 0)) &&
         !__any_sync(0xffffffffu, *abort_flag != 0)) {
@@ -405,7 +431,12 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
 #pragma unroll
       for (int c = 0; c < 128; ++c) v[c] *= p.scale;
       if (key < p.kv_len) {
-        if (p.rope.pos != nullptr) rope_rotate_row128(p.rope, key, v, true);
+        if (p.rope.pos != nullptr) {
+          if (p.rope.axis_dim == 32 && p.rope.n_axes == 4)
+            rope_rotate_row128_ax32(p.rope, key, v, true);
+          else
+            rope_rotate_row128(p.rope, key, v, true);
+        }
         store_row(p, true, b, key, h, v);
       }
     } else {
@@ -432,11 +463,18 @@ int launch_attn_bwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
                          float* dk_acc, float* dv_acc, float scale,
                          const fa_rope_t* rope, const float2* rope_table,
                          cudaStream_t stream) {
-  CUtensorMap tq, tk, tv, tdo;
+  CUtensorMap tq, tk, tv, tdo, tdq;
   int rc = make_tmap_bshd(&tq, q, sh.B, sh.S, sh.H, sh.D, 128);
   if (!rc) rc = make_tmap_bshd(&tk, k, sh.B, kv_len, sh.H, sh.D, 128);
   if (!rc) rc = make_tmap_bshd(&tv, v, sh.B, kv_len, sh.H, sh.D, 128);
   if (!rc) rc = make_tmap_bshd(&tdo, d_o, sh.B, sh.S, sh.H, sh.D, 128);
+  fa_tensor_t dqa;
+  dqa.data = dq_acc;
+  dqa.stride_d = 1;
+  dqa.stride_h = sh.D;
+  dqa.stride_s = (int64_t)sh.H * sh.D;
+  dqa.stride_b = (int64_t)sh.S * sh.H * sh.D;
+  if (!rc) rc = make_tmap_bshd_f32(&tdq, &dqa, sh.B, sh.S, sh.H, sh.D, 128);
   if (rc) return rc;
   bwd::Params p;
   p.S = sh.S;
@@ -467,7 +505,7 @@ int launch_attn_bwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
   if (rc) return rc;
   dim3 grid((kv_len + 127) / 128, sh.H, sh.B);
   bwd::attn_bwd_kernel<<<grid, bwd::kThreads, bwd::kSmemBytes, stream>>>(
-      tq, tk, tv, tdo, p);
+      tq, tk, tv, tdo, tdq, p);
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 

@@ -64,12 +64,6 @@ struct Params {
   float* lse;  // (B, H, S)
 };
 
-__device__ __forceinline__ float fast_exp2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
 __global__ void __launch_bounds__(kThreads, 1)
 attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                 const __grid_constant__ CUtensorMap tm_k,
@@ -262,20 +256,21 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
           }
         }
       }
-      float sum = 0.f;
+      float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
       for (int cb = 0; cb < 4; ++cb) {
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float p0 = fast_exp2(fmaf(sv[cb * 32 + 2 * i], sl2, -m_use));
-          const float p1 =
-              fast_exp2(fmaf(sv[cb * 32 + 2 * i + 1], sl2, -m_use));
-          sum += p0 + p1;
-          pk[i] = pack_bf16(p0, p1);
+          const float p0 = exp2_mixed<0>(fmaf(sv[cb * 32 + 2 * i], sl2, -m_use));
+          const float p1 = exp2_mixed<1>(fmaf(sv[cb * 32 + 2 * i + 1], sl2, -m_use));
+          sum0 += p0;
+          sum1 += p1;
+          pk[i] = pack_bf16_alu(p0, p1);
         }
         tmem_st16(t_p + cb * 16, pk);
       }
+      const float sum = sum0 + sum1;
       tmem_wait_st();
       l_run = l_run * alpha + sum;
       m_run = m_use;

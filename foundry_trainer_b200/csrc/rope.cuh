@@ -82,4 +82,27 @@ __device__ __forceinline__ void rope_rotate_row128(const RopeArgs& r,
   }
 }
 
+// Same, for the reference layout (axes of 32 columns covering head_dim 128):
+// fully unrolled so the row stays in registers.
+__device__ __forceinline__ void rope_rotate_row128_ax32(const RopeArgs& r,
+                                                        int token, float* v,
+                                                        bool inverse) {
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float2 cs = rope_cs(r, token, a * 16 + j);
+      const float x1 = v[a * 32 + j];
+      const float x2 = v[a * 32 + j + 16];
+      if (!inverse) {
+        v[a * 32 + j] = __fadd_rn(__fmul_rn(x1, cs.x), __fmul_rn(-x2, cs.y));
+        v[a * 32 + j + 16] = __fadd_rn(__fmul_rn(x2, cs.x), __fmul_rn(x1, cs.y));
+      } else {
+        v[a * 32 + j] = __fadd_rn(__fmul_rn(x1, cs.x), __fmul_rn(x2, cs.y));
+        v[a * 32 + j + 16] = __fadd_rn(__fmul_rn(x2, cs.x), __fmul_rn(-x1, cs.y));
+      }
+    }
+  }
+}
+
 }  // namespace fa

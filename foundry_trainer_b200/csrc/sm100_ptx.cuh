@@ -100,6 +100,28 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map,
       : "memory");
 }
 
+// 4-D tiled reduce-add (fp32) of a shared-memory tile into global memory.
+__device__ __forceinline__ void tma_reduce_add_4d(const CUtensorMap* map,
+                                                  const void* src, int c0,
+                                                  int c1, int c2, int c3) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.4d.global.shared::cta.add.tile.bulk_group "
+      "[%0, {%2, %3, %4, %5}], [%1];" ::"l"(reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Waits until every committed bulk group has finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_group_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Waits until every committed bulk group has completed.
+__device__ __forceinline__ void bulk_wait_group0() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 // Orders this thread's generic-proxy shared-memory writes before later
 // async-proxy (TMA / tensor core) reads of the same memory.
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -281,6 +303,47 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// Two fp32 -> packed bf16x2 (lo in bits 0-15) with round-to-nearest-even,
+// done with integer ALU ops so it does not compete with the exponentials for
+// the XU (transcendental / conversion) pipe. Inputs are finite.
+__device__ __forceinline__ uint32_t pack_bf16_alu(float lo, float hi) {
+  uint32_t a = __float_as_uint(lo), b = __float_as_uint(hi);
+  a += 0x7FFFu + ((a >> 16) & 1u);
+  b += 0x7FFFu + ((b >> 16) & 1u);
+  return __byte_perm(a, b, 0x7632);
+}
+
+// 2^x on the FMA pipe: x = n + f with n = round(x), f in [-1/2, 1/2];
+// 2^f by a cubic fitted for minimax relative error on [-1/2, 1/2]
+// (Lawson-reweighted least squares on Chebyshev nodes; max relative error
+// 7.5e-5 evaluated in fp32, below bf16 resolution); 2^n added to the
+// exponent field. Returns 0 for x < -125 (and for x = -inf).
+__device__ __forceinline__ float exp2_poly(float x) {
+  const float xc = fmaxf(x, -125.f);
+  const float t = xc + 12582912.f;  // 1.5 * 2^23: the add rounds xc to an integer
+  const int n = __float_as_int(t) - 0x4B400000;
+  const float f = xc - (t - 12582912.f);
+  float p = fmaf(0.0551716648f, f, 0.242611125f);
+  p = fmaf(p, f, 0.693260968f);
+  p = fmaf(p, f, 0.999928057f);
+  const float r = __int_as_float(__float_as_int(p) + (int)((unsigned)n << 23));
+  return x < -125.f ? 0.f : r;
+}
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Exponential split between the XU pipe (MUFU ex2) and the FMA pipe
+// (polynomial): element index i uses the polynomial when i is odd, so the two
+// pipes share the work of a row.
+template <int I>
+__device__ __forceinline__ float exp2_mixed(float x) {
+  return (I & 1) ? exp2_poly(x) : fast_exp2(x);
+}
+
 __device__ __forceinline__ float bf16_lo(uint32_t v) {
   return __uint_as_float(v << 16);
 }
@@ -299,6 +362,22 @@ __device__ __forceinline__ bool elect_one() {
       "selp.u32 %0, 1, 0, P;\n\t}"
       : "=r"(pred));
   return pred != 0;
+}
+
+// Named barrier over `nthreads` threads that also ORs a predicate across
+// them: every participant gets the same answer, so a group can leave a loop
+// together (no participant is left waiting at a later named barrier).
+__device__ __forceinline__ bool named_bar_any(int id, int nthreads, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 q, %1, 0;\n\t"
+      "bar.red.or.pred p, %2, %3, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
 }
 
 // Named barrier over `nthreads` threads (a multiple of 32).
