@@ -11,18 +11,22 @@
 // rounded to bf16 for the tensor core with fp32 accumulation.
 //
 // One CTA owns one 128-key K/V tile of one (b, h) and walks all 128-row Q
-// tiles (K/V stationary):
-//   warp 8      TMA producer: K, V once; Q_i, dO_i, LSE_i, Delta_i per step
-//   warp 9      tcgen05 MMA issuer, TMEM owner
-//   warps 0-3   softmax backward, one key row per thread; dV epilogue
-//   warps 4-7   dQ drain: TMEM -> swizzled shared tile -> TMA bulk reduce-add
-//               (fp32) into dq_acc; dK epilogue
+// tiles (K/V stationary). 14 warps:
+//   warp 8        TMA producer: K, V once; Q_i, dO_i, LSE_i, Delta_i per step
+//   warp 9        tcgen05 MMA issuer, TMEM owner
+//   warps 0-3     softmax backward for queries 0-63 of the tile (one key row
+//                 per thread); dV epilogue
+//   warps 10-13   the same for queries 64-127; dK epilogue
+//   warps 4-7     dQ drain: TMEM -> swizzled shared tile -> TMA bulk
+//                 reduce-add (fp32) into dq_acc
 // TMEM (512 columns):
-//   A [0,128)    S^T_i, then P^T_i (bf16, cols 0-63) | dS^T_i (bf16, 64-127)
+//   A [0,128)    S^T_i; after the softmax, per query half h (columns
+//                64h..64h+63): P^T (bf16 pairs, 32 columns) then dS^T (32
+//                columns) — each half only overwrites columns it has read
 //   B [128,256)  dP^T_i, then dQ_i (fp32, query rows)
 //   dV [256,384) dK [384,512)   accumulators over all Q tiles
 // Every MMA that overwrites columns another MMA reads waits for that MMA's
-// commit first; dQ_i is drained while S^T_{i+1} runs. The dQ drain stages
+// commit first; dQ_i is drained while S^T_{i+1} runs. The drain stages
 // through the dS^T shared tile (free once the dQ MMA has read it) and hands it
 // back to the softmax warps (DSFREE) when the bulk reduce has read it.
 #include "attn_common.h"
@@ -35,7 +39,7 @@ namespace bwd {
 constexpr int kRows = 128;
 constexpr int kTileBytes = 32768;
 constexpr int kBlkBytes = 16384;
-constexpr int kThreads = 320;
+constexpr int kThreads = 448;
 
 constexpr int kOffK = 0;
 constexpr int kOffV = kOffK + kTileBytes;
@@ -70,7 +74,6 @@ struct Params {
   float scale, scale_log2;
   const float* lse2_pad;    // (B, H, s_pad): LSE * log2(e), +inf padding
   const float* delta_pad;   // (B, H, s_pad): rowsum(dO*O), 0 padding
-  float* dq_acc;            // (B, S, H, D) fp32, zeroed by the caller
   // dK / dV output: bf16 strided tensors, or fp32 accumulators when acc != 0
   int acc;
   __nv_bfloat16* dk;
@@ -91,15 +94,16 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src,
       : "memory");
 }
 
-// Writes one 128-value fp32 row held in registers to a dK/dV destination.
-__device__ __forceinline__ void store_row(const Params& p, bool is_dk, int b,
-                                          int key, int h, float* v) {
+// Writes columns [col0, col0+64) of one dK/dV row held in registers.
+__device__ __forceinline__ void store_half_row(const Params& p, bool is_dk,
+                                               int b, int key, int h, int col0,
+                                               const float* v) {
   if (p.acc) {
     float* dst = (is_dk ? p.dk_acc : p.dv_acc) +
-                 (((int64_t)b * p.kv_len + key) * p.H + h) * 128;
+                 (((int64_t)b * p.kv_len + key) * p.H + h) * 128 + col0;
     float4* d4 = reinterpret_cast<float4*>(dst);
 #pragma unroll
-    for (int c = 0; c < 32; ++c) {
+    for (int c = 0; c < 16; ++c) {
       float4 o = d4[c];
       o.x += v[4 * c + 0];
       o.y += v[4 * c + 1];
@@ -109,13 +113,14 @@ __device__ __forceinline__ void store_row(const Params& p, bool is_dk, int b,
     }
   } else {
     __nv_bfloat16* dst =
-        is_dk ? p.dk + (int64_t)b * p.dks_b + (int64_t)key * p.dks_s +
-                    (int64_t)h * p.dks_h
-              : p.dv + (int64_t)b * p.dvs_b + (int64_t)key * p.dvs_s +
-                    (int64_t)h * p.dvs_h;
+        (is_dk ? p.dk + (int64_t)b * p.dks_b + (int64_t)key * p.dks_s +
+                     (int64_t)h * p.dks_h
+               : p.dv + (int64_t)b * p.dvs_b + (int64_t)key * p.dvs_s +
+                     (int64_t)h * p.dvs_h) +
+        col0;
     uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-    for (int c = 0; c < 16; ++c) {
+    for (int c = 0; c < 8; ++c) {
       uint4 o;
       o.x = pack_bf16(v[8 * c + 0], v[8 * c + 1]);
       o.y = pack_bf16(v[8 * c + 2], v[8 * c + 3]);
@@ -126,7 +131,23 @@ __device__ __forceinline__ void store_row(const Params& p, bool is_dk, int b,
   }
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+// Inverse rotation of columns [col0, col0+64) (two 32-wide axis segments).
+__device__ __forceinline__ void unrotate_half_row(const RopeArgs& r, int token,
+                                                  int col0, float* v) {
+#pragma unroll
+  for (int a = 0; a < 2; ++a) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float2 cs = rope_cs(r, token, (col0 / 32 + a) * 16 + j);
+      const float x1 = v[a * 32 + j];
+      const float x2 = v[a * 32 + j + 16];
+      v[a * 32 + j] = __fadd_rn(__fmul_rn(x1, cs.x), __fmul_rn(x2, cs.y));
+      v[a * 32 + j + 16] = __fadd_rn(__fmul_rn(x2, cs.x), __fmul_rn(-x1, cs.y));
+    }
+  }
+}
+
+__global__ void __maxnreg__(144)
 attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                 const __grid_constant__ CUtensorMap tm_k,
                 const __grid_constant__ CUtensorMap tm_v,
@@ -157,7 +178,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
       mbar_init(&bars[B_QEMPTY + s], 1);
     }
     mbar_init(&bars[B_SDP], 1);
-    mbar_init(&bars[B_PS], 128);
+    mbar_init(&bars[B_PS], 256);
     mbar_init(&bars[B_DQFULL], 1);
     mbar_init(&bars[B_DQFREE], 128);
     mbar_init(&bars[B_DVK], 1);
@@ -245,15 +266,17 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
         umma_commit(&bars[B_SDP]);
         if (!(ok = mbar_wait(&bars[B_PS], i & 1))) break;
         tc_fence_after();
-        // dV += P^T dO_i ; dK += dS^T Q_i   (A operands from TMEM)
+        // dV += P^T dO_i ; dK += dS^T Q_i   (A operands from TMEM; K slice kk
+        // is queries 16kk..16kk+15: half kk>>2, eight packed columns each)
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          umma_ts(tmem + kColDV, tmem + kColA + kk * 8,
+          umma_ts(tmem + kColDV, tmem + kColA + (kk >> 2) * 64 + (kk & 3) * 8,
                   mnmajor_desc(do_base, kk, kBlkBytes), kIdKM,
                   (i > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          umma_ts(tmem + kColDK, tmem + kColA + 64 + kk * 8,
+          umma_ts(tmem + kColDK,
+                  tmem + kColA + (kk >> 2) * 64 + 32 + (kk & 3) * 8,
                   mnmajor_desc(q_base, kk, kBlkBytes), kIdKM,
                   (i > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&bars[B_DVK]);
@@ -269,13 +292,15 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
       umma_commit(&bars[B_FINAL]);
       mbar_wait(&bars[B_FINAL], 0);
     }
-  } else if (warp < 4) {
-    // ----------------------------------------- softmax backward (key rows)
-    const int key_in_tile = warp * 32 + lane;
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-    const uint32_t t_a = tmem + lane_off + kColA;
-    const uint32_t t_b = tmem + lane_off + kColB;
-    uint8_t* ds_row = smem + kOffDS;
+  } else if (warp < 4 || warp >= 10) {
+    // ------------------------------- softmax backward (key rows, query half)
+    const int half = warp >= 10 ? 1 : 0;
+    const int sub = warp & 3;
+    const int key_in_tile = sub * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(sub * 32) << 16;
+    const uint32_t t_a = tmem + lane_off + kColA + (uint32_t)half * 64u;
+    const uint32_t t_b = tmem + lane_off + kColB + (uint32_t)half * 64u;
+    uint8_t* ds_blk = smem + kOffDS + half * kBlkBytes;
     const float sl2 = p.scale_log2;
     bool ok = true;
     for (int i = 0; i < nq; ++i) {
@@ -287,54 +312,50 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
       ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_QFULL + st], n & 1));
       if (!ok) break;
       tc_fence_after();
-      const float4* lse4 = reinterpret_cast<const float4*>(smem + kOffLse + st * 512);
-      const float4* dlt4 = reinterpret_cast<const float4*>(smem + kOffDelta + st * 512);
-      // S^T columns 64-127 are read first: dS^T of query chunks 0-3 is
-      // written over them (columns 64-127), P^T of chunk c over S^T columns
-      // 16c..16c+15, which chunk c (or an earlier one) has already read.
-      uint32_t s_hi[64];
-      tmem_ld32(t_a + 64, s_hi);
-      tmem_ld32(t_a + 96, s_hi + 32);
+      const float4* lse4 =
+          reinterpret_cast<const float4*>(smem + kOffLse + st * 512) + half * 16;
+      const float4* dlt4 =
+          reinterpret_cast<const float4*>(smem + kOffDelta + st * 512) + half * 16;
+      // this half's S^T columns, all read before any is overwritten
+      uint32_t sr[64];
+      tmem_ld32(t_a + 0, sr);
+      tmem_ld32(t_a + 32, sr + 32);
       // the drain of dQ_{i-1} must have released the shared dS^T tile
       if (i > 0) {
         ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_DSFREE], (i - 1) & 1));
         if (!ok) break;
       }
 #pragma unroll
-      for (int cb = 0; cb < 4; ++cb) {
-        uint32_t s_lo[32], dr[32];
-        if (cb < 2) tmem_ld32(t_a + cb * 32, s_lo);
+      for (int cb = 0; cb < 2; ++cb) {
+        uint32_t dr[32];
         tmem_ld32(t_b + cb * 32, dr);
         tmem_wait_ld();
-        const uint32_t* sr = cb < 2 ? s_lo : s_hi + (cb - 2) * 32;
         uint32_t pk[16], dk[16];
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
           const float4 l = lse4[cb * 8 + u];
           const float4 dl = dlt4[cb * 8 + u];
-          const int c = 4 * u;
-          const float p0 = exp2_mixed<0>(fmaf(__uint_as_float(sr[c + 0]), sl2, -l.x));
-          const float p1 = exp2_mixed<1>(fmaf(__uint_as_float(sr[c + 1]), sl2, -l.y));
-          const float p2 = exp2_mixed<0>(fmaf(__uint_as_float(sr[c + 2]), sl2, -l.z));
-          const float p3 = exp2_mixed<1>(fmaf(__uint_as_float(sr[c + 3]), sl2, -l.w));
-          pk[2 * u] = pack_bf16_alu(p0, p1);
-          pk[2 * u + 1] = pack_bf16_alu(p2, p3);
-          const float d0 = p0 * (__uint_as_float(dr[c + 0]) - dl.x);
-          const float d1 = p1 * (__uint_as_float(dr[c + 1]) - dl.y);
-          const float d2 = p2 * (__uint_as_float(dr[c + 2]) - dl.z);
-          const float d3 = p3 * (__uint_as_float(dr[c + 3]) - dl.w);
-          dk[2 * u] = pack_bf16_alu(d0, d1);
-          dk[2 * u + 1] = pack_bf16_alu(d2, d3);
+          const int c = cb * 32 + 4 * u;
+          const int e = 4 * u;
+          const float p0 = fast_exp2(fmaf(__uint_as_float(sr[c + 0]), sl2, -l.x));
+          const float p1 = fast_exp2(fmaf(__uint_as_float(sr[c + 1]), sl2, -l.y));
+          const float p2 = fast_exp2(fmaf(__uint_as_float(sr[c + 2]), sl2, -l.z));
+          const float p3 = fast_exp2(fmaf(__uint_as_float(sr[c + 3]), sl2, -l.w));
+          pk[2 * u] = pack_bf16(p0, p1);
+          pk[2 * u + 1] = pack_bf16(p2, p3);
+          dk[2 * u] = pack_bf16(p0 * (__uint_as_float(dr[e + 0]) - dl.x),
+                                p1 * (__uint_as_float(dr[e + 1]) - dl.y));
+          dk[2 * u + 1] = pack_bf16(p2 * (__uint_as_float(dr[e + 2]) - dl.z),
+                                    p3 * (__uint_as_float(dr[e + 3]) - dl.w));
         }
-        tmem_st16(t_a + cb * 16, pk);
-        tmem_st16(t_a + 64 + cb * 16, dk);
-        // dS^T row -> shared memory: queries [32cb, 32cb+32) are 16-byte
-        // chunks 4*(cb&1) .. +3 of swizzle block cb>>1.
-        uint8_t* blk = ds_row + (cb >> 1) * kBlkBytes;
+        tmem_st16(t_a + cb * 16, pk);       // P^T: columns 64h + [0, 32)
+        tmem_st16(t_a + 32 + cb * 16, dk);  // dS^T: columns 64h + [32, 64)
+        // dS^T row -> shared memory: queries 64h + [32cb, 32cb+32) are
+        // 16-byte chunks 4cb .. 4cb+3 of swizzle block h.
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const uint32_t off = sw128_offset(key_in_tile, (cb & 1) * 4 + u);
-          *reinterpret_cast<uint4*>(blk + off) =
+          const uint32_t off = sw128_offset(key_in_tile, cb * 4 + u);
+          *reinterpret_cast<uint4*>(ds_blk + off) =
               make_uint4(dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
         }
       }
@@ -343,19 +364,29 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
       tc_fence_before();
       mbar_arrive(&bars[B_PS]);
     }
-    // dV epilogue
+    // epilogue: warps 0-3 store dV, warps 10-13 store dK (scaled, and
+    // un-rotated when the op owns the RoPE), 64 columns at a time
     if (ok && __all_sync(0xffffffffu, mbar_wait(&bars[B_FINAL], 0)) &&
         !__any_sync(0xffffffffu, *abort_flag != 0)) {
       tc_fence_after();
-      uint32_t r[128];
-      const uint32_t t_dv = tmem + lane_off + kColDV;
-      tmem_ld32(t_dv + 0, r);
-      tmem_ld32(t_dv + 32, r + 32);
-      tmem_ld32(t_dv + 64, r + 64);
-      tmem_ld32(t_dv + 96, r + 96);
-      tmem_wait_ld();
+      const bool is_dk = half == 1;
+      const uint32_t t_acc = tmem + lane_off + (is_dk ? kColDK : kColDV);
       const int key = kv_tile * kRows + key_in_tile;
-      if (key < p.kv_len) store_row(p, false, b, key, h, reinterpret_cast<float*>(r));
+#pragma unroll
+      for (int hc = 0; hc < 2; ++hc) {
+        uint32_t r[64];
+        tmem_ld32(t_acc + hc * 64, r);
+        tmem_ld32(t_acc + hc * 64 + 32, r + 32);
+        tmem_wait_ld();
+        float* v = reinterpret_cast<float*>(r);
+        if (is_dk) {
+#pragma unroll
+          for (int c = 0; c < 64; ++c) v[c] *= p.scale;
+          if (p.rope.pos != nullptr && key < p.kv_len)
+            unrotate_half_row(p.rope, key, hc * 64, v);
+        }
+        if (key < p.kv_len) store_half_row(p, is_dk, b, key, h, hc * 64, v);
+      }
     } else {
       *abort_flag = 1;
     }
@@ -367,81 +398,61 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
     const uint32_t t_b = tmem + lane_off + kColB;
     const bool leader = (warp == 4 && lane == 0);
     uint8_t* stage = smem + kOffDS;  // two 16 KB boxes of 32 fp32 columns
-    bool ok = true;
     for (int i = 0; i < nq; ++i) {
       // leave together: the passes below use a named barrier over warps 4-7
       bool stop = *abort_flag != 0;
       if (!stop) stop = !mbar_wait(&bars[B_DQFULL], i & 1);
-      if (named_bar_any(2, 128, stop)) { ok = false; break; }
+      if (named_bar_any(2, 128, stop)) break;
       tc_fence_after();
-      uint32_t r[128];
-      tmem_ld32(t_b + 0, r);
-      tmem_ld32(t_b + 32, r + 32);
-      tmem_ld32(t_b + 64, r + 64);
-      tmem_ld32(t_b + 96, r + 96);
+      // pass 0: columns 0-63 through the shared tile (the dQ MMA, its only
+      // other reader, has completed: DQFULL)
+      uint32_t r0[32], r1[32];
+      tmem_ld32(t_b + 0, r0);
+      tmem_ld32(t_b + 32, r1);
+      tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint32_t off = sw128_offset(row_in_tile, c);
+        *reinterpret_cast<uint4*>(stage + off) =
+            make_uint4(r0[4 * c], r0[4 * c + 1], r0[4 * c + 2], r0[4 * c + 3]);
+        *reinterpret_cast<uint4*>(stage + kBlkBytes + off) =
+            make_uint4(r1[4 * c], r1[4 * c + 1], r1[4 * c + 2], r1[4 * c + 3]);
+      }
+      // columns 64-127 into registers; then TMEM B can take dP^T_{i+1}
+      tmem_ld32(t_b + 64, r0);
+      tmem_ld32(t_b + 96, r1);
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(&bars[B_DQFREE]);
-      // two passes of 64 columns through the 32 KB dS^T tile (the dQ MMA,
-      // its only reader, has completed: DQFULL)
-#pragma unroll
-      for (int pass = 0; pass < 2; ++pass) {
-        if (pass == 1) {
-          // the first pass's bulk reduce must have read the tile
-          if (leader) bulk_wait_group_read0();
-          named_bar_sync(2, 128);
-        }
-#pragma unroll
-        for (int bx = 0; bx < 2; ++bx) {
-          uint8_t* box = stage + bx * kBlkBytes;
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            const int col = pass * 64 + bx * 32 + c * 4;
-            *reinterpret_cast<uint4*>(box + sw128_offset(row_in_tile, c)) =
-                make_uint4(r[col], r[col + 1], r[col + 2], r[col + 3]);
-          }
-        }
-        fence_proxy_async_smem();
-        named_bar_sync(2, 128);
-        if (leader) {
-          tma_reduce_add_4d(&tm_dq, stage, pass * 64, i * kRows, h, b);
-          tma_reduce_add_4d(&tm_dq, stage + kBlkBytes, pass * 64 + 32, i * kRows, h, b);
-          bulk_commit_group();
-        }
-      }
+      fence_proxy_async_smem();
+      named_bar_sync(2, 128);
       if (leader) {
+        tma_reduce_add_4d(&tm_dq, stage, 0, i * kRows, h, b);
+        tma_reduce_add_4d(&tm_dq, stage + kBlkBytes, 32, i * kRows, h, b);
+        bulk_commit_group();
+        bulk_wait_group_read0();
+      }
+      named_bar_sync(2, 128);
+      // pass 1: columns 64-127
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint32_t off = sw128_offset(row_in_tile, c);
+        *reinterpret_cast<uint4*>(stage + off) =
+            make_uint4(r0[4 * c], r0[4 * c + 1], r0[4 * c + 2], r0[4 * c + 3]);
+        *reinterpret_cast<uint4*>(stage + kBlkBytes + off) =
+            make_uint4(r1[4 * c], r1[4 * c + 1], r1[4 * c + 2], r1[4 * c + 3]);
+      }
+      fence_proxy_async_smem();
+      named_bar_sync(2, 128);
+      if (leader) {
+        tma_reduce_add_4d(&tm_dq, stage, 64, i * kRows, h, b);
+        tma_reduce_add_4d(&tm_dq, stage + kBlkBytes, 96, i * kRows, h, b);
+        bulk_commit_group();
         bulk_wait_group_read0();
         mbar_arrive(&bars[B_DSFREE]);
       }
     }
     if (leader) bulk_wait_group0();  // reductions complete before exit
-    // dK epilogue: scale, inverse rotation (when the op owns the RoPE)
-    if (ok && __all_sync(0xffffffffu, mbar_wait(&bars[B_FINAL], 0)) &&
-        !__any_sync(0xffffffffu, *abort_flag != 0)) {
-      tc_fence_after();
-      uint32_t r[128];
-      const uint32_t t_dk = tmem + lane_off + kColDK;
-      tmem_ld32(t_dk + 0, r);
-      tmem_ld32(t_dk + 32, r + 32);
-      tmem_ld32(t_dk + 64, r + 64);
-      tmem_ld32(t_dk + 96, r + 96);
-      tmem_wait_ld();
-      const int key = kv_tile * kRows + row_in_tile;
-      float* v = reinterpret_cast<float*>(r);
-#pragma unroll
-      for (int c = 0; c < 128; ++c) v[c] *= p.scale;
-      if (key < p.kv_len) {
-        if (p.rope.pos != nullptr) {
-          if (p.rope.axis_dim == 32 && p.rope.n_axes == 4)
-            rope_rotate_row128_ax32(p.rope, key, v, true);
-          else
-            rope_rotate_row128(p.rope, key, v, true);
-        }
-        store_row(p, true, b, key, h, v);
-      }
-    } else {
-      *abort_flag = 1;
-    }
   }
 
   tc_fence_before();
@@ -463,6 +474,8 @@ int launch_attn_bwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
                          float* dk_acc, float* dv_acc, float scale,
                          const fa_rope_t* rope, const float2* rope_table,
                          cudaStream_t stream) {
+  if (rope != nullptr && (rope->axis_dim != 32 || rope->n_axes != 4))
+    return FA_ERR_UNSUPPORTED;  // the dK epilogue un-rotates 32-wide axes
   CUtensorMap tq, tk, tv, tdo, tdq;
   int rc = make_tmap_bshd(&tq, q, sh.B, sh.S, sh.H, sh.D, 128);
   if (!rc) rc = make_tmap_bshd(&tk, k, sh.B, kv_len, sh.H, sh.D, 128);
@@ -486,7 +499,6 @@ int launch_attn_bwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
   p.scale_log2 = scale * 1.4426950408889634f;
   p.lse2_pad = lse2_pad;
   p.delta_pad = delta_pad;
-  p.dq_acc = dq_acc;
   p.acc = (dk_acc != nullptr) ? 1 : 0;
   p.dk = dk ? reinterpret_cast<__nv_bfloat16*>(dk->data) : nullptr;
   p.dks_b = dk ? dk->stride_b : 0;

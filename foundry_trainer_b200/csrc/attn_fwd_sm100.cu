@@ -10,9 +10,11 @@
 //
 // One CTA owns one 128-row Q tile of one (b, h) and streams 128-key K/V
 // tiles through TMA rings (K: 2 stages, V: 3 stages):
-//   warp 4      TMA producer (one lane)
-//   warp 5      tcgen05 MMA issuer (one lane), TMEM owner
-//   warps 0-3   softmax, O rescale and epilogue (one Q row per thread)
+//   warp 8      TMA producer (one lane)
+//   warp 9      tcgen05 MMA issuer (one lane), TMEM owner
+//   warps 0-7   softmax, O rescale and epilogue: two warpgroups, each thread
+//               owns half a Q row (warpgroup 0 keys/columns 0-63, warpgroup 1
+//               64-127); the row maximum is combined through shared memory.
 // TMEM (512 columns allocated): S_a [0,128) S_b [128,256) P [256,320)
 // O [384,512). S is double-buffered so S(j+1) = Q K_{j+1}^T runs on the tensor
 // core while the softmax of tile j runs; P (bf16, two per column) is the TMEM
@@ -30,7 +32,7 @@ constexpr int kTileBytes = 32768;   // 128 x 128 bf16
 constexpr int kBlkBytes = 16384;    // one 64-column swizzle block
 constexpr int kKStages = 2;
 constexpr int kVStages = 3;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
 
 // shared memory map (offsets from a 1024-byte aligned base)
 constexpr int kOffQ = 0;
@@ -38,7 +40,10 @@ constexpr int kOffK = kOffQ + kTileBytes;
 constexpr int kOffV = kOffK + kKStages * kTileBytes;
 constexpr int kOffBar = kOffV + kVStages * kTileBytes;
 constexpr int kNumBars = 20;
-constexpr int kOffMisc = kOffBar + kNumBars * 8;
+// [3][2][128] fp32: row maxima of the two halves for even / odd KV tiles, then
+// the two halves' row sums for the epilogue
+constexpr int kOffRed = kOffBar + kNumBars * 8;
+constexpr int kOffMisc = kOffRed + 3 * 2 * 128 * 4;
 constexpr int kSmemBytes = kOffMisc + 64 + 1024;  // + alignment slack
 
 // barrier indices
@@ -95,13 +100,13 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
     }
     mbar_init(&bars[B_SFULL + 0], 1);
     mbar_init(&bars[B_SFULL + 1], 1);
-    mbar_init(&bars[B_PREADY], 128);
+    mbar_init(&bars[B_PREADY], 256);
     mbar_init(&bars[B_PVDONE], 1);
     mbar_init(&bars[B_FINAL], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -110,7 +115,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
@@ -149,7 +154,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
       }
       if (!ok) *abort_flag = 1;
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ----------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t kIdescS = idesc_bf16(128, 128, false, false);
@@ -197,37 +202,47 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
       mbar_wait(&bars[B_FINAL], 0);
     }
   } else {
-    // ------------------------------------------------ softmax warpgroup
-    const int row_in_tile = warp * 32 + lane;
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-    const uint32_t t_p = tmem + lane_off + kColP;
-    const uint32_t t_o = tmem + lane_off + kColO;
+    // ----------------------------------------------- softmax warpgroups
+    const int wg = warp >> 2;                 // column half of the row
+    const int sub = warp & 3;                 // TMEM lane quarter
+    const int row_in_tile = sub * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(sub * 32) << 16;
+    const uint32_t t_p = tmem + lane_off + kColP + (uint32_t)wg * 32u;
+    const uint32_t t_o = tmem + lane_off + kColO + (uint32_t)wg * 64u;
+    float* red = reinterpret_cast<float*>(smem + kOffRed);  // [j&1][wg][row]
     const float sl2 = p.scale_log2;
     float m_run = -INFINITY;
-    float l_run = 0.f;
-    bool ok = true;
+    float l_run = 0.f;  // this half's share of the row sum
+    bool failed = false;
     for (int j = 0; j < nkv; ++j) {
-      if (__any_sync(0xffffffffu, *abort_flag != 0)) { ok = false; break; }
-      ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_SFULL + (j & 1)], (j >> 1) & 1));
-      if (!ok) break;
-      tc_fence_after();
-      const uint32_t t_s = tmem + lane_off + kColS + (uint32_t)(j & 1) * 128u;
-      uint32_t sr[128];
-      tmem_ld32(t_s + 0, sr);
-      tmem_ld32(t_s + 32, sr + 32);
-      tmem_ld32(t_s + 64, sr + 64);
-      tmem_ld32(t_s + 96, sr + 96);
-      tmem_wait_ld();
-      float* sv = reinterpret_cast<float*>(sr);
-      const int valid = p.S - j * kKeys;
-      if (valid < kKeys) {
+      bool stop = failed || *abort_flag != 0;
+      if (!stop) stop = !mbar_wait(&bars[B_SFULL + (j & 1)], (j >> 1) & 1);
+      stop = __any_sync(0xffffffffu, stop);
+      uint32_t sr[64];
+      float mx = -INFINITY;
+      if (!stop) {
+        tc_fence_after();
+        const uint32_t t_s =
+            tmem + lane_off + kColS + (uint32_t)(j & 1) * 128u + (uint32_t)wg * 64u;
+        tmem_ld32(t_s + 0, sr);
+        tmem_ld32(t_s + 32, sr + 32);
+        tmem_wait_ld();
+        float* sv = reinterpret_cast<float*>(sr);
+        const int valid = p.S - j * kKeys - wg * 64;
+        if (valid < 64) {
 #pragma unroll
-        for (int c = 0; c < 128; ++c)
-          if (c >= valid) sv[c] = -INFINITY;
+          for (int c = 0; c < 64; ++c)
+            if (c >= valid) sv[c] = -INFINITY;
+        }
+        mx = sv[0];
+#pragma unroll
+        for (int c = 1; c < 64; ++c) mx = fmaxf(mx, sv[c]);
+        red[((j & 1) * 2 + wg) * 128 + row_in_tile] = mx;
       }
-      float mx = sv[0];
-#pragma unroll
-      for (int c = 1; c < 128; ++c) mx = fmaxf(mx, sv[c]);
+      // both halves leave together; after this the partner's maximum is visible
+      if (named_bar_any(1, 256, stop)) break;
+      mx = fmaxf(mx, red[((j & 1) * 2 + (wg ^ 1)) * 128 + row_in_tile]);
+      float* sv = reinterpret_cast<float*>(sr);
       const float m_cand = mx * sl2;
       float m_use = m_run;
       float alpha = 1.f;
@@ -240,12 +255,14 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
       }
       // P and O are free once PV(j-1) has completed.
       if (j > 0) {
-        ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_PVDONE], (j - 1) & 1));
-        if (!ok) break;
+        if (!__all_sync(0xffffffffu, mbar_wait(&bars[B_PVDONE], (j - 1) & 1))) {
+          failed = true;
+          continue;
+        }
         tc_fence_after();
         if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
-          for (int cb = 0; cb < 4; ++cb) {
+          for (int cb = 0; cb < 2; ++cb) {
             uint32_t orow[32];
             tmem_ld32(t_o + cb * 32, orow);
             tmem_wait_ld();
@@ -258,42 +275,45 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
       }
       float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
-      for (int cb = 0; cb < 4; ++cb) {
+      for (int cb = 0; cb < 2; ++cb) {
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float p0 = exp2_mixed<0>(fmaf(sv[cb * 32 + 2 * i], sl2, -m_use));
-          const float p1 = exp2_mixed<1>(fmaf(sv[cb * 32 + 2 * i + 1], sl2, -m_use));
+          const float p0 = fast_exp2(fmaf(sv[cb * 32 + 2 * i], sl2, -m_use));
+          const float p1 = fast_exp2(fmaf(sv[cb * 32 + 2 * i + 1], sl2, -m_use));
           sum0 += p0;
           sum1 += p1;
-          pk[i] = pack_bf16_alu(p0, p1);
+          pk[i] = pack_bf16(p0, p1);
         }
         tmem_st16(t_p + cb * 16, pk);
       }
-      const float sum = sum0 + sum1;
       tmem_wait_st();
-      l_run = l_run * alpha + sum;
+      l_run = l_run * alpha + (sum0 + sum1);
       m_run = m_use;
       tc_fence_before();
       mbar_arrive(&bars[B_PREADY]);
     }
-    if (ok && !__any_sync(0xffffffffu, *abort_flag != 0) &&
-        __all_sync(0xffffffffu, mbar_wait(&bars[B_PVDONE], (nkv - 1) & 1))) {
+    // epilogue: combine the two halves' row sums, then each half stores its
+    // 64 output columns
+    bool stop = failed || *abort_flag != 0;
+    if (!stop) stop = !mbar_wait(&bars[B_PVDONE], (nkv - 1) & 1);
+    stop = __any_sync(0xffffffffu, stop);
+    if (!stop) red[(4 + wg) * 128 + row_in_tile] = l_run;
+    if (!named_bar_any(1, 256, stop)) {
       tc_fence_after();
+      const float l_tot = l_run + red[(4 + (wg ^ 1)) * 128 + row_in_tile];
       const int row = q_tile * kRows + row_in_tile;
-      const float inv_l = 1.f / l_run;
-      uint32_t orow[128];
+      const float inv_l = 1.f / l_tot;
+      uint32_t orow[64];
       tmem_ld32(t_o + 0, orow);
       tmem_ld32(t_o + 32, orow + 32);
-      tmem_ld32(t_o + 64, orow + 64);
-      tmem_ld32(t_o + 96, orow + 96);
       tmem_wait_ld();
       if (row < p.S) {
         __nv_bfloat16* dst = p.o + (int64_t)b * p.os_b + (int64_t)row * p.os_s +
-                             (int64_t)h * p.os_h;
+                             (int64_t)h * p.os_h + wg * 64;
         uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
+        for (int c = 0; c < 8; ++c) {
           uint4 v;
           v.x = pack_bf16(__uint_as_float(orow[c * 8 + 0]) * inv_l,
                           __uint_as_float(orow[c * 8 + 1]) * inv_l);
@@ -305,8 +325,9 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                           __uint_as_float(orow[c * 8 + 7]) * inv_l);
           d4[c] = v;
         }
-        p.lse[((int64_t)b * p.H + h) * p.S + row] =
-            (m_run + __log2f(l_run)) * 0.69314718055994531f;
+        if (wg == 0)
+          p.lse[((int64_t)b * p.H + h) * p.S + row] =
+              (m_run + __log2f(l_tot)) * 0.69314718055994531f;
       }
     } else {
       *abort_flag = 1;
@@ -315,7 +336,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, 512);
