@@ -73,6 +73,7 @@ SIGNATURES = {
     "fa_timing_enable": (C.c_int, [C.c_int]),
     "fa_timing_read": (C.c_int, [C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_int)]),
     "fa_status_string": (C.c_char_p, [C.c_int]),
+    "fa_last_error": (C.c_char_p, []),
     "fa_device_status": (C.c_int, []),
     "fa_abi_version": (C.c_int, []),
     "fa_build_info": (C.c_char_p, []),
@@ -116,7 +117,10 @@ def status_string(status: int) -> str:
 
 def check(status: int, where: str) -> None:
     if status != FA_OK:
-        raise FaError(status, where, status_string(status))
+        msg = status_string(status)
+        if status == FA_ERR_LAUNCH:
+            msg += f" [{load().fa_last_error().decode()}]"
+        raise FaError(status, where, msg)
 
 
 def loaded_path() -> str:

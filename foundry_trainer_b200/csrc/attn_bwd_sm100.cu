@@ -147,7 +147,7 @@ __device__ __forceinline__ void unrotate_half_row(const RopeArgs& r, int token,
   }
 }
 
-__global__ void __maxnreg__(144)
+__global__ void __launch_bounds__(kThreads, 1)
 attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                 const __grid_constant__ CUtensorMap tm_k,
                 const __grid_constant__ CUtensorMap tm_v,
@@ -316,26 +316,29 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
           reinterpret_cast<const float4*>(smem + kOffLse + st * 512) + half * 16;
       const float4* dlt4 =
           reinterpret_cast<const float4*>(smem + kOffDelta + st * 512) + half * 16;
-      // this half's S^T columns, all read before any is overwritten
-      uint32_t sr[64];
-      tmem_ld32(t_a + 0, sr);
-      tmem_ld32(t_a + 32, sr + 32);
+      // This half's S^T columns 32-63 are read first: dS^T (columns 32-63)
+      // is written over them; P^T of chunk c goes over columns 8c..8c+7,
+      // which chunk c or an earlier chunk has already read.
+      uint32_t s_hi[32];
+      tmem_ld32(t_a + 32, s_hi);
       // the drain of dQ_{i-1} must have released the shared dS^T tile
       if (i > 0) {
         ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_DSFREE], (i - 1) & 1));
         if (!ok) break;
       }
 #pragma unroll
-      for (int cb = 0; cb < 2; ++cb) {
-        uint32_t dr[32];
-        tmem_ld32(t_b + cb * 32, dr);
+      for (int cb = 0; cb < 4; ++cb) {
+        uint32_t dr[16], s_lo[16];
+        if (cb < 2) tmem_ld16(t_a + cb * 16, s_lo);
+        tmem_ld16(t_b + cb * 16, dr);
         tmem_wait_ld();
-        uint32_t pk[16], dk[16];
+        const uint32_t* sr = cb < 2 ? s_lo : s_hi + (cb - 2) * 16;
+        uint32_t pk[8], dk[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const float4 l = lse4[cb * 8 + u];
-          const float4 dl = dlt4[cb * 8 + u];
-          const int c = cb * 32 + 4 * u;
+        for (int u = 0; u < 4; ++u) {
+          const float4 l = lse4[cb * 4 + u];
+          const float4 dl = dlt4[cb * 4 + u];
+          const int c = 4 * u;
           const int e = 4 * u;
           const float p0 = fast_exp2(fmaf(__uint_as_float(sr[c + 0]), sl2, -l.x));
           const float p1 = fast_exp2(fmaf(__uint_as_float(sr[c + 1]), sl2, -l.y));
@@ -348,13 +351,13 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
           dk[2 * u + 1] = pack_bf16(p2 * (__uint_as_float(dr[e + 2]) - dl.z),
                                     p3 * (__uint_as_float(dr[e + 3]) - dl.w));
         }
-        tmem_st16(t_a + cb * 16, pk);       // P^T: columns 64h + [0, 32)
-        tmem_st16(t_a + 32 + cb * 16, dk);  // dS^T: columns 64h + [32, 64)
-        // dS^T row -> shared memory: queries 64h + [32cb, 32cb+32) are
-        // 16-byte chunks 4cb .. 4cb+3 of swizzle block h.
+        tmem_st8(t_a + cb * 8, pk);       // P^T: columns 64h + [0, 32)
+        tmem_st8(t_a + 32 + cb * 8, dk);  // dS^T: columns 64h + [32, 64)
+        // dS^T row -> shared memory: queries 64h + [16cb, 16cb+16) are
+        // 16-byte chunks 2cb, 2cb+1 of swizzle block h.
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const uint32_t off = sw128_offset(key_in_tile, cb * 4 + u);
+        for (int u = 0; u < 2; ++u) {
+          const uint32_t off = sw128_offset(key_in_tile, cb * 2 + u);
           *reinterpret_cast<uint4*>(ds_blk + off) =
               make_uint4(dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
         }
@@ -518,7 +521,7 @@ int launch_attn_bwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
   dim3 grid((kv_len + 127) / 128, sh.H, sh.B);
   bwd::attn_bwd_kernel<<<grid, bwd::kThreads, bwd::kSmemBytes, stream>>>(
       tq, tk, tv, tdo, tdq, p);
-  return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+  return launch_status();
 }
 
 }  // namespace fa

@@ -33,6 +33,12 @@ enum KernelId {
   kKernelCount = 8
 };
 
+// FA_OK when the last CUDA runtime call / launch on this thread succeeded;
+// otherwise records the CUDA error text (see fa_last_error) and returns
+// FA_ERR_LAUNCH.
+int launch_status();
+int record_cuda_error(cudaError_t e);
+
 // Raises the dynamic shared-memory limit of `fn` once per (device, kernel).
 int ensure_smem_attr(const void* fn, int bytes, int kernel_id);
 

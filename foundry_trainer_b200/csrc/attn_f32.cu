@@ -256,7 +256,7 @@ int launch_attn_fwd_f32(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
   f32::fwd_kernel<<<grid, f32::kThreads, smem, stream>>>(
       f32::view_of(q), f32::view_of(k), f32::view_of(v), f32::outview_of(o),
       lse, sh.S, kv_len, sh.H, scale);
-  return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+  return launch_status();
 }
 
 int launch_attn_bwd_f32(const AttnShape& sh, const fa_tensor_t* q,
@@ -276,11 +276,11 @@ int launch_attn_bwd_f32(const AttnShape& sh, const fa_tensor_t* q,
   f32::dkdv_kernel<<<grid, f32::kThreads, smem_kv, stream>>>(
       f32::view_of(q), f32::view_of(k), f32::view_of(v), f32::view_of(d_o),
       lse, delta, f32::outview_of(dk), f32::outview_of(dv), sh.S, sh.H, scale);
-  if (cudaGetLastError() != cudaSuccess) return FA_ERR_LAUNCH;
+  if (launch_status() != FA_OK) return FA_ERR_LAUNCH;
   f32::dq_kernel<<<grid, f32::kThreads, smem_q, stream>>>(
       f32::view_of(q), f32::view_of(k), f32::view_of(v), f32::view_of(d_o),
       lse, delta, f32::outview_of(dq), sh.S, sh.H, scale);
-  return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+  return launch_status();
 }
 
 }  // namespace fa

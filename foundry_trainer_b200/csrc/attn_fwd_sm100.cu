@@ -372,7 +372,7 @@ int launch_attn_fwd_bf16(const AttnShape& sh, const fa_tensor_t* q,
   dim3 grid((sh.S + fwd::kRows - 1) / fwd::kRows, sh.H, sh.B);
   fwd::attn_fwd_kernel<<<grid, fwd::kThreads, fwd::kSmemBytes, stream>>>(
       tq, tk, tv, p);
-  return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+  return launch_status();
 }
 
 }  // namespace fa

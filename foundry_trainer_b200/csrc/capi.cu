@@ -5,6 +5,7 @@
 
 #include <atomic>
 #include <cmath>
+#include <cstdio>
 #include <cstring>
 #include <mutex>
 #include <utility>
@@ -72,6 +73,18 @@ int make_tmap_bshd_f32(CUtensorMap* map, const fa_tensor_t* t, int B, int S,
                      CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, 32);
 }
 
+// ------------------------------------------------------ CUDA error text
+static thread_local char g_last_error[256] = "";
+
+int record_cuda_error(cudaError_t e) {
+  if (e == cudaSuccess) return FA_OK;
+  std::snprintf(g_last_error, sizeof(g_last_error), "%s: %s", cudaGetErrorName(e),
+                cudaGetErrorString(e));
+  return FA_ERR_LAUNCH;
+}
+
+int launch_status() { return record_cuda_error(cudaGetLastError()); }
+
 // ------------------------------------------------- per-device attributes
 static std::atomic<int> g_attr_done[64][kKernelCount];
 
@@ -80,9 +93,9 @@ int ensure_smem_attr(const void* fn, int bytes, int kernel_id) {
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
     return FA_ERR_NO_DEVICE;
   if (g_attr_done[dev][kernel_id].load(std::memory_order_acquire)) return FA_OK;
-  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           bytes) != cudaSuccess)
-    return FA_ERR_LAUNCH;
+  const cudaError_t e =
+      cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return record_cuda_error(e);
   g_attr_done[dev][kernel_id].store(1, std::memory_order_release);
   return FA_OK;
 }
@@ -226,6 +239,8 @@ const char* fa_status_string(int status) {
 }
 
 int fa_abi_version(void) { return FA_ABI_VERSION; }
+
+const char* fa_last_error(void) { return g_last_error; }
 
 const char* fa_build_info(void) {
   return "foundry_attn sm_100a (tcgen05/TMEM/TMA bf16 path, fp32 SIMT path)";

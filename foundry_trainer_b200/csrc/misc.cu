@@ -185,7 +185,7 @@ int launch_bwd_delta(int dtype, const AttnShape& sh, const fa_tensor_t* o,
   else
     misc::delta_kernel<float><<<grid, 32 * misc::kWarps, 0, stream>>>(
         misc::tview(o), misc::tview(d_o), lse, delta, lse2, sh.S, sh.H, s_pad, sh.B);
-  return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+  return launch_status();
 }
 
 static int launch_rope_generic(int dtype_in, int dtype_out, const AttnShape& sh,
@@ -225,7 +225,7 @@ static int launch_rope_generic(int dtype_in, int dtype_out, const AttnShape& sh,
     else FA_ROPE_R(__nv_bfloat16, float);
 #undef FA_ROPE_R
   }
-  return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+  return launch_status();
 }
 
 int launch_rope_table(int dtype, int S, const fa_rope_t* rope, int pos_offset,
@@ -233,7 +233,7 @@ int launch_rope_table(int dtype, int S, const fa_rope_t* rope, int pos_offset,
   const RopeArgs r = make_rope_args(rope, dtype == FA_DTYPE_BF16 ? 1 : 0, pos_offset);
   const int64_t n = (int64_t)S * r.n_axes * (r.axis_dim / 2);
   misc::rope_table_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(r, S, table);
-  return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+  return launch_status();
 }
 
 int launch_rope(int dtype, const AttnShape& sh, const fa_tensor_t* x,
@@ -279,7 +279,7 @@ int launch_lse_merge(int dtype, const AttnShape& sh, float* o_acc,
   else
     misc::lse_merge_kernel<float><<<grid, 32 * misc::kWarps, 0, stream>>>(
         o_acc, lse_acc, misc::tview(o_blk), lse_blk, sh.S, sh.H, sh.B, first);
-  return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+  return launch_status();
 }
 
 }  // namespace fa

@@ -178,6 +178,10 @@ int fa_timing_read(int kernel, double* total_ms, int* launches);
 /* Human-readable name of a status code. Never NULL. */
 const char* fa_status_string(int status);
 
+/* The CUDA error behind the last FA_ERR_LAUNCH on the calling thread ("" if
+ * none). Never NULL. */
+const char* fa_last_error(void);
+
 /*
  * Reads and clears the device status word of the current device that the
  * kernels set when a bounded wait expires (0 when clean). Synchronises the
