@@ -17,18 +17,19 @@
 //   warps 0-3     softmax backward for queries 0-63 of the tile (one key row
 //                 per thread); dV epilogue
 //   warps 10-13   the same for queries 64-127; dK epilogue
-//   warps 4-7     dQ drain: TMEM -> swizzled shared tile -> TMA bulk
-//                 reduce-add (fp32) into dq_acc
+//   warps 4-7     dQ drain: dQ^T rows from TMEM, reduced into dq_acc with
+//                 coalesced fp32 red (a warp adds 32 consecutive floats)
 // TMEM (512 columns):
 //   A [0,128)    S^T_i; after the softmax, per query half h (columns
 //                64h..64h+63): P^T (bf16 pairs, 32 columns) then dS^T (32
 //                columns) — each half only overwrites columns it has read
-//   B [128,256)  dP^T_i, then dQ_i (fp32, query rows)
+//   B [128,256)  dP^T_i, then dQ^T_i = K^T dS^T_i (fp32; lane = head-dim
+//                column, column = query)
 //   dV [256,384) dK [384,512)   accumulators over all Q tiles
 // Every MMA that overwrites columns another MMA reads waits for that MMA's
-// commit first; dQ_i is drained while S^T_{i+1} runs. The drain stages
-// through the dS^T shared tile (free once the dQ MMA has read it) and hands it
-// back to the softmax warps (DSFREE) when the bulk reduce has read it.
+// commit first; dQ_i is drained while S^T_{i+1} runs. The shared dS^T tile is
+// rewritten by the softmax of step i+1 only after S^T/dP^T of step i+1
+// complete, and their commit covers the dQ^T_i MMA that read it.
 #include "attn_common.h"
 #include "rope.cuh"
 #include "sm100_ptx.cuh"
@@ -62,7 +63,6 @@ constexpr int B_DQFULL = 7;
 constexpr int B_DQFREE = 8;
 constexpr int B_DVK = 9;
 constexpr int B_FINAL = 10;
-constexpr int B_DSFREE = 11;
 
 constexpr uint32_t kColA = 0;
 constexpr uint32_t kColB = 128;
@@ -82,8 +82,13 @@ struct Params {
   int64_t dvs_b, dvs_s, dvs_h;
   float* dk_acc;            // (B, kv_len, H, D) fp32
   float* dv_acc;
+  float* dq_acc;            // (B, S, H, D) fp32, zeroed by the caller
   RopeArgs rope;            // rope.pos == nullptr: no rotation
 };
+
+__device__ __forceinline__ void red_add_f32(float* addr, float v) {
+  asm volatile("red.global.add.f32 [%0], %1;" ::"l"(addr), "f"(v) : "memory");
+}
 
 __device__ __forceinline__ void bulk_load(void* dst, const void* src,
                                           uint32_t bytes, uint64_t* bar) {
@@ -151,8 +156,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                 const __grid_constant__ CUtensorMap tm_k,
                 const __grid_constant__ CUtensorMap tm_v,
-                const __grid_constant__ CUtensorMap tm_do,
-                const __grid_constant__ CUtensorMap tm_dq, Params p) {
+                const __grid_constant__ CUtensorMap tm_do, Params p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc);
@@ -183,7 +187,6 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
     mbar_init(&bars[B_DQFREE], 128);
     mbar_init(&bars[B_DVK], 1);
     mbar_init(&bars[B_FINAL], 1);
-    mbar_init(&bars[B_DSFREE], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -281,11 +284,11 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                   (i > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&bars[B_DVK]);
         umma_commit(&bars[B_QEMPTY + st]);
-        // dQ_i = dS_i K -> B   (dS from shared memory, query-major view)
+        // dQ^T_i = K^T dS^T_i -> B   (both operands MN-major in shared memory)
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          umma_ss(tmem + kColB, mnmajor_desc(ds_base, kk, kBlkBytes),
-                  mnmajor_desc(k_base, kk, kBlkBytes), kIdMM, kk > 0);
+          umma_ss(tmem + kColB, mnmajor_desc(k_base, kk, kBlkBytes),
+                  mnmajor_desc(ds_base, kk, kBlkBytes), kIdMM, kk > 0);
         umma_commit(&bars[B_DQFULL]);
       }
       if (!ok) *abort_flag = 1;
@@ -321,11 +324,6 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
       // which chunk c or an earlier chunk has already read.
       uint32_t s_hi[32];
       tmem_ld32(t_a + 32, s_hi);
-      // the drain of dQ_{i-1} must have released the shared dS^T tile
-      if (i > 0) {
-        ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_DSFREE], (i - 1) & 1));
-        if (!ok) break;
-      }
 #pragma unroll
       for (int cb = 0; cb < 4; ++cb) {
         uint32_t dr[16], s_lo[16];
@@ -394,68 +392,44 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
       *abort_flag = 1;
     }
   } else {
-    // ------------------------------------------ dQ drain (query rows)
+    // ------------------------------ dQ drain (head-dim column per thread)
     const int sub = warp & 3;
-    const int row_in_tile = sub * 32 + lane;
+    const int d = sub * 32 + lane;
     const uint32_t lane_off = (uint32_t)(sub * 32) << 16;
     const uint32_t t_b = tmem + lane_off + kColB;
-    const bool leader = (warp == 4 && lane == 0);
-    uint8_t* stage = smem + kOffDS;  // two 16 KB boxes of 32 fp32 columns
+    float* dq_col = p.dq_acc + (((int64_t)b * p.S) * p.H + h) * 128 + d;
+    const int64_t q_stride = (int64_t)p.H * 128;
+    // a warp's 32 lanes add 32 consecutive floats of one dQ row
+    auto reduce_chunk = [&](const uint32_t* v, int q0) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (q0 + j < p.S)
+          red_add_f32(dq_col + (int64_t)(q0 + j) * q_stride, __uint_as_float(v[j]));
+    };
+    bool ok = true;
     for (int i = 0; i < nq; ++i) {
-      // leave together: the passes below use a named barrier over warps 4-7
-      bool stop = *abort_flag != 0;
-      if (!stop) stop = !mbar_wait(&bars[B_DQFULL], i & 1);
-      if (named_bar_any(2, 128, stop)) break;
+      if (__any_sync(0xffffffffu, *abort_flag != 0)) { ok = false; break; }
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_DQFULL], i & 1));
+      if (!ok) break;
       tc_fence_after();
-      // pass 0: columns 0-63 through the shared tile (the dQ MMA, its only
-      // other reader, has completed: DQFULL)
+      const int q0 = i * kRows;
       uint32_t r0[32], r1[32];
       tmem_ld32(t_b + 0, r0);
       tmem_ld32(t_b + 32, r1);
       tmem_wait_ld();
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint32_t off = sw128_offset(row_in_tile, c);
-        *reinterpret_cast<uint4*>(stage + off) =
-            make_uint4(r0[4 * c], r0[4 * c + 1], r0[4 * c + 2], r0[4 * c + 3]);
-        *reinterpret_cast<uint4*>(stage + kBlkBytes + off) =
-            make_uint4(r1[4 * c], r1[4 * c + 1], r1[4 * c + 2], r1[4 * c + 3]);
-      }
-      // columns 64-127 into registers; then TMEM B can take dP^T_{i+1}
+      reduce_chunk(r0, q0);
       tmem_ld32(t_b + 64, r0);
+      tmem_wait_ld();
+      reduce_chunk(r1, q0 + 32);
       tmem_ld32(t_b + 96, r1);
       tmem_wait_ld();
+      // every column of dQ^T_i is in registers: B can take dP^T_{i+1}
       tc_fence_before();
       mbar_arrive(&bars[B_DQFREE]);
-      fence_proxy_async_smem();
-      named_bar_sync(2, 128);
-      if (leader) {
-        tma_reduce_add_4d(&tm_dq, stage, 0, i * kRows, h, b);
-        tma_reduce_add_4d(&tm_dq, stage + kBlkBytes, 32, i * kRows, h, b);
-        bulk_commit_group();
-        bulk_wait_group_read0();
-      }
-      named_bar_sync(2, 128);
-      // pass 1: columns 64-127
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint32_t off = sw128_offset(row_in_tile, c);
-        *reinterpret_cast<uint4*>(stage + off) =
-            make_uint4(r0[4 * c], r0[4 * c + 1], r0[4 * c + 2], r0[4 * c + 3]);
-        *reinterpret_cast<uint4*>(stage + kBlkBytes + off) =
-            make_uint4(r1[4 * c], r1[4 * c + 1], r1[4 * c + 2], r1[4 * c + 3]);
-      }
-      fence_proxy_async_smem();
-      named_bar_sync(2, 128);
-      if (leader) {
-        tma_reduce_add_4d(&tm_dq, stage, 64, i * kRows, h, b);
-        tma_reduce_add_4d(&tm_dq, stage + kBlkBytes, 96, i * kRows, h, b);
-        bulk_commit_group();
-        bulk_wait_group_read0();
-        mbar_arrive(&bars[B_DSFREE]);
-      }
+      reduce_chunk(r0, q0 + 64);
+      reduce_chunk(r1, q0 + 96);
     }
-    if (leader) bulk_wait_group0();  // reductions complete before exit
+    if (!ok) *abort_flag = 1;
   }
 
   tc_fence_before();
@@ -479,18 +453,11 @@ int launch_attn_bwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
                          cudaStream_t stream) {
   if (rope != nullptr && (rope->axis_dim != 32 || rope->n_axes != 4))
     return FA_ERR_UNSUPPORTED;  // the dK epilogue un-rotates 32-wide axes
-  CUtensorMap tq, tk, tv, tdo, tdq;
+  CUtensorMap tq, tk, tv, tdo;
   int rc = make_tmap_bshd(&tq, q, sh.B, sh.S, sh.H, sh.D, 128);
   if (!rc) rc = make_tmap_bshd(&tk, k, sh.B, kv_len, sh.H, sh.D, 128);
   if (!rc) rc = make_tmap_bshd(&tv, v, sh.B, kv_len, sh.H, sh.D, 128);
   if (!rc) rc = make_tmap_bshd(&tdo, d_o, sh.B, sh.S, sh.H, sh.D, 128);
-  fa_tensor_t dqa;
-  dqa.data = dq_acc;
-  dqa.stride_d = 1;
-  dqa.stride_h = sh.D;
-  dqa.stride_s = (int64_t)sh.H * sh.D;
-  dqa.stride_b = (int64_t)sh.S * sh.H * sh.D;
-  if (!rc) rc = make_tmap_bshd_f32(&tdq, &dqa, sh.B, sh.S, sh.H, sh.D, 128);
   if (rc) return rc;
   bwd::Params p;
   p.S = sh.S;
@@ -513,6 +480,7 @@ int launch_attn_bwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
   p.dvs_h = dv ? dv->stride_h : 0;
   p.dk_acc = dk_acc;
   p.dv_acc = dv_acc;
+  p.dq_acc = dq_acc;
   p.rope = make_rope_args(rope);
   p.rope.table = rope_table;
   rc = ensure_smem_attr((const void*)bwd::attn_bwd_kernel, bwd::kSmemBytes,
@@ -520,7 +488,7 @@ int launch_attn_bwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
   if (rc) return rc;
   dim3 grid((kv_len + 127) / 128, sh.H, sh.B);
   bwd::attn_bwd_kernel<<<grid, bwd::kThreads, bwd::kSmemBytes, stream>>>(
-      tq, tk, tv, tdo, tdq, p);
+      tq, tk, tv, tdo, p);
   return launch_status();
 }
 

@@ -15,11 +15,11 @@
 //   warps 0-7   softmax, O rescale and epilogue: two warpgroups, each thread
 //               owns half a Q row (warpgroup 0 keys/columns 0-63, warpgroup 1
 //               64-127); the row maximum is combined through shared memory.
-// TMEM (512 columns allocated): S_a [0,128) S_b [128,256) P [256,320)
-// O [384,512). S is double-buffered so S(j+1) = Q K_{j+1}^T runs on the tensor
-// core while the softmax of tile j runs; P (bf16, two per column) is the TMEM
-// A operand of O += P V and has its own columns, so no MMA ever has to wait
-// for another MMA to drain.
+// TMEM (512 columns): S_a [0,128) S_b [128,256) P_a [256,320) P_b [320,384)
+// O [384,512). S and P are double-buffered: S(j+1) = Q K_{j+1}^T runs on the
+// tensor core while the softmax of tile j runs, and the softmax of tile j+1
+// writes its P (bf16, two per column; the TMEM A operand of O += P V) while
+// PV(j) still reads the other buffer. No MMA waits for another to drain.
 #include "attn_common.h"
 #include "sm100_ptx.cuh"
 
@@ -53,12 +53,12 @@ constexpr int B_KEMPTY = 3;   // + stage (2)
 constexpr int B_VFULL = 5;    // + stage (3)
 constexpr int B_VEMPTY = 8;   // + stage (3)
 constexpr int B_SFULL = 11;   // + S buffer (2)
-constexpr int B_PREADY = 13;  // softmax wrote P(j) (and finished reading S(j))
-constexpr int B_PVDONE = 14;  // O += P(j) V_j completed
-constexpr int B_FINAL = 15;
+constexpr int B_PREADY = 13;  // + P buffer (2): softmax wrote P(j), read S(j)
+constexpr int B_PVDONE = 15;  // + P buffer (2): O += P(j) V_j completed
+constexpr int B_FINAL = 17;
 
 constexpr uint32_t kColS = 0;
-constexpr uint32_t kColP = 256;
+constexpr uint32_t kColP = 256;  // + 64 * (j & 1)
 constexpr uint32_t kColO = 384;
 
 struct Params {
@@ -100,8 +100,10 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
     }
     mbar_init(&bars[B_SFULL + 0], 1);
     mbar_init(&bars[B_SFULL + 1], 1);
-    mbar_init(&bars[B_PREADY], 256);
-    mbar_init(&bars[B_PVDONE], 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&bars[B_PREADY + t], 256);
+      mbar_init(&bars[B_PVDONE + t], 1);
+    }
     mbar_init(&bars[B_FINAL], 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -183,15 +185,16 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
         if (*abort_flag) { ok = false; break; }
         const int s = j % kVStages, n = j / kVStages;
         if (!(ok = mbar_wait(&bars[B_VFULL + s], n & 1))) break;
-        if (!(ok = mbar_wait(&bars[B_PREADY], j & 1))) break;
+        if (!(ok = mbar_wait(&bars[B_PREADY + (j & 1)], (j >> 1) & 1))) break;
         tc_fence_after();
         const uint32_t v_base = smem_u32(smem + kOffV + s * kTileBytes);
+        const uint32_t p_col = kColP + (uint32_t)(j & 1) * 64u;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          umma_ts(tmem + kColO, tmem + kColP + kk * 8,
+          umma_ts(tmem + kColO, tmem + p_col + kk * 8,
                   mnmajor_desc(v_base, kk, kBlkBytes), kIdescO,
                   (j > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&bars[B_PVDONE]);
+        umma_commit(&bars[B_PVDONE + (j & 1)]);
         umma_commit(&bars[B_VEMPTY + s]);
         // S buffer j&1 was read by softmax(j) before it signalled P ready.
         if (j + 2 < nkv) ok = issue_s(j + 2);
@@ -207,7 +210,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
     const int sub = warp & 3;                 // TMEM lane quarter
     const int row_in_tile = sub * 32 + lane;
     const uint32_t lane_off = (uint32_t)(sub * 32) << 16;
-    const uint32_t t_p = tmem + lane_off + kColP + (uint32_t)wg * 32u;
+    const uint32_t t_p0 = tmem + lane_off + kColP + (uint32_t)wg * 32u;
     const uint32_t t_o = tmem + lane_off + kColO + (uint32_t)wg * 64u;
     float* red = reinterpret_cast<float*>(smem + kOffRed);  // [j&1][wg][row]
     const float sl2 = p.scale_log2;
@@ -253,50 +256,56 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
         m_use = m_cand;
         alpha = fast_exp2(m_run - m_cand);  // 0 when m_run == -inf
       }
-      // P and O are free once PV(j-1) has completed.
-      if (j > 0) {
-        if (!__all_sync(0xffffffffu, mbar_wait(&bars[B_PVDONE], (j - 1) & 1))) {
+      float sum0 = 0.f, sum1 = 0.f;
+      uint32_t pk[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float p0 = fast_exp2(fmaf(sv[2 * i], sl2, -m_use));
+        const float p1 = fast_exp2(fmaf(sv[2 * i + 1], sl2, -m_use));
+        sum0 += p0;
+        sum1 += p1;
+        pk[i] = pack_bf16(p0, p1);
+      }
+      // P buffer j&1 is free once PV(j-2) has completed.
+      if (j >= 2 && !__all_sync(0xffffffffu, mbar_wait(&bars[B_PVDONE + (j & 1)],
+                                                        ((j - 2) >> 1) & 1))) {
+        failed = true;
+        continue;
+      }
+      // O may only be rescaled while no PV is in flight: after PV(j-1).
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&bars[B_PVDONE + ((j - 1) & 1)],
+                                               ((j - 1) >> 1) & 1))) {
           failed = true;
           continue;
         }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
-          for (int cb = 0; cb < 2; ++cb) {
-            uint32_t orow[32];
-            tmem_ld32(t_o + cb * 32, orow);
-            tmem_wait_ld();
+        for (int cb = 0; cb < 4; ++cb) {
+          uint32_t orow[16];
+          tmem_ld16(t_o + cb * 16, orow);
+          tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-              orow[i] = __float_as_uint(__uint_as_float(orow[i]) * alpha);
-            tmem_st32(t_o + cb * 32, orow);
-          }
+          for (int i = 0; i < 16; ++i)
+            orow[i] = __float_as_uint(__uint_as_float(orow[i]) * alpha);
+          tmem_st16(t_o + cb * 16, orow);
         }
       }
-      float sum0 = 0.f, sum1 = 0.f;
-#pragma unroll
-      for (int cb = 0; cb < 2; ++cb) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float p0 = fast_exp2(fmaf(sv[cb * 32 + 2 * i], sl2, -m_use));
-          const float p1 = fast_exp2(fmaf(sv[cb * 32 + 2 * i + 1], sl2, -m_use));
-          sum0 += p0;
-          sum1 += p1;
-          pk[i] = pack_bf16(p0, p1);
-        }
-        tmem_st16(t_p + cb * 16, pk);
-      }
+      tc_fence_after();
+      const uint32_t t_p = t_p0 + (uint32_t)(j & 1) * 64u;
+      tmem_st16(t_p, pk);
+      tmem_st16(t_p + 16, pk + 16);
       tmem_wait_st();
       l_run = l_run * alpha + (sum0 + sum1);
       m_run = m_use;
       tc_fence_before();
-      mbar_arrive(&bars[B_PREADY]);
+      mbar_arrive(&bars[B_PREADY + (j & 1)]);
     }
     // epilogue: combine the two halves' row sums, then each half stores its
     // 64 output columns
     bool stop = failed || *abort_flag != 0;
-    if (!stop) stop = !mbar_wait(&bars[B_PVDONE], (nkv - 1) & 1);
+    if (!stop)
+      stop = !mbar_wait(&bars[B_PVDONE + ((nkv - 1) & 1)], ((nkv - 1) >> 1) & 1);
     stop = __any_sync(0xffffffffu, stop);
     if (!stop) red[(4 + wg) * 128 + row_in_tile] = l_run;
     if (!named_bar_any(1, 256, stop)) {
