@@ -11,14 +11,17 @@
 // rounded to bf16 for the tensor core with fp32 accumulation.
 //
 // One CTA owns one 128-key K/V tile of one (b, h) and walks all 128-row Q
-// tiles (K/V stationary). 14 warps:
+// tiles (K/V stationary), starting at Q tile `kv_tile` and wrapping, so the
+// CTAs of one head add into different dQ rows at any moment instead of all
+// contending for the same L2 lines. 14 warps:
 //   warp 8        TMA producer: K, V once; Q_i, dO_i, LSE_i, Delta_i per step
 //   warp 9        tcgen05 MMA issuer, TMEM owner
 //   warps 0-3     softmax backward for queries 0-63 of the tile (one key row
 //                 per thread); dV epilogue
 //   warps 10-13   the same for queries 64-127; dK epilogue
-//   warps 4-7     dQ drain: dQ^T rows from TMEM, reduced into dq_acc with
-//                 coalesced fp32 red (a warp adds 32 consecutive floats)
+//   warps 4-7     dQ drain: dQ^T from TMEM, staged as row-major 32-query
+//                 chunks in shared memory, added into dq_acc (B, H, S_pad, D)
+//                 with 16 KB TMA bulk reduce-adds (fp32)
 // TMEM (512 columns):
 //   A [0,128)    S^T_i; after the softmax, per query half h (columns
 //                64h..64h+63): P^T (bf16 pairs, 32 columns) then dS^T (32
@@ -27,9 +30,9 @@
 //                column, column = query)
 //   dV [256,384) dK [384,512)   accumulators over all Q tiles
 // Every MMA that overwrites columns another MMA reads waits for that MMA's
-// commit first; dQ_i is drained while S^T_{i+1} runs. The shared dS^T tile is
-// rewritten by the softmax of step i+1 only after S^T/dP^T of step i+1
-// complete, and their commit covers the dQ^T_i MMA that read it.
+// commit first; dQ_i is drained while S^T_{i+1} runs. The drain stages through
+// the shared dS^T tile (free once the dQ^T MMA has read it: DQFULL) and hands
+// it back to the softmax warps (DSFREE) once the bulk reduces have read it.
 #include "attn_common.h"
 #include "rope.cuh"
 #include "sm100_ptx.cuh"
@@ -63,6 +66,7 @@ constexpr int B_DQFULL = 7;
 constexpr int B_DQFREE = 8;
 constexpr int B_DVK = 9;
 constexpr int B_FINAL = 10;
+constexpr int B_DSFREE = 11;
 
 constexpr uint32_t kColA = 0;
 constexpr uint32_t kColB = 128;
@@ -82,12 +86,24 @@ struct Params {
   int64_t dvs_b, dvs_s, dvs_h;
   float* dk_acc;            // (B, kv_len, H, D) fp32
   float* dv_acc;
-  float* dq_acc;            // (B, S, H, D) fp32, zeroed by the caller
+  float* dq_acc;            // (B, H, s_pad, D) fp32, zeroed by the caller
   RopeArgs rope;            // rope.pos == nullptr: no rotation
 };
 
-__device__ __forceinline__ void red_add_f32(float* addr, float v) {
-  asm volatile("red.global.add.f32 [%0], %1;" ::"l"(addr), "f"(v) : "memory");
+// Q tile visited at step i by the CTA of K/V tile `kv_tile`.
+__device__ __forceinline__ int q_tile_of(int i, int kv_tile, int nq) {
+  const int t = i + kv_tile % nq;
+  return t >= nq ? t - nq : t;
+}
+
+// dst[0 .. bytes/4) += src[...] (fp32), performed by the TMA unit.
+__device__ __forceinline__ void bulk_reduce_add_f32(float* dst, const float* src,
+                                                    uint32_t bytes) {
+  asm volatile(
+      "cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;" ::"l"(
+          dst),
+      "r"(smem_u32(src)), "r"(bytes)
+      : "memory");
 }
 
 __device__ __forceinline__ void bulk_load(void* dst, const void* src,
@@ -187,6 +203,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
     mbar_init(&bars[B_DQFREE], 128);
     mbar_init(&bars[B_DVK], 1);
     mbar_init(&bars[B_FINAL], 1);
+    mbar_init(&bars[B_DSFREE], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -219,7 +236,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
         if (*abort_flag) break;
         if (i >= 2 && !(ok = mbar_wait(&bars[B_QEMPTY + st], (n - 1) & 1)))
           break;
-        const int qrow = i * kRows;
+        const int qrow = q_tile_of(i, kv_tile, nq) * kRows;
         uint64_t* bar = &bars[B_QFULL + st];
         mbar_arrive_expect_tx(bar, 2 * kTileBytes + 1024);
         uint8_t* qd = smem + kOffQ + st * kTileBytes;
@@ -324,6 +341,11 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
       // which chunk c or an earlier chunk has already read.
       uint32_t s_hi[32];
       tmem_ld32(t_a + 32, s_hi);
+      // the drain of dQ_{i-1} must have released the shared dS^T tile
+      if (i > 0) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_DSFREE], (i - 1) & 1));
+        if (!ok) break;
+      }
 #pragma unroll
       for (int cb = 0; cb < 4; ++cb) {
         uint32_t dr[16], s_lo[16];
@@ -397,39 +419,57 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
     const int d = sub * 32 + lane;
     const uint32_t lane_off = (uint32_t)(sub * 32) << 16;
     const uint32_t t_b = tmem + lane_off + kColB;
-    float* dq_col = p.dq_acc + (((int64_t)b * p.S) * p.H + h) * 128 + d;
-    const int64_t q_stride = (int64_t)p.H * 128;
-    // a warp's 32 lanes add 32 consecutive floats of one dQ row
-    auto reduce_chunk = [&](const uint32_t* v, int q0) {
+    const bool leader = (warp == 4 && lane == 0);
+    // two 16 KB staging chunks (32 queries x 128 fp32, row-major) in the
+    // shared dS^T tile; a thread writes column d, a warp 128 contiguous bytes
+    float* stage_a = reinterpret_cast<float*>(smem + kOffDS);
+    float* stage_b = stage_a + 32 * 128;
+    float* dq_bh = p.dq_acc + ((int64_t)b * p.H + h) * p.s_pad * 128;
+    auto stage = [&](float* buf, const uint32_t* v) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (q0 + j < p.S)
-          red_add_f32(dq_col + (int64_t)(q0 + j) * q_stride, __uint_as_float(v[j]));
+      for (int j = 0; j < 32; ++j) buf[j * 128 + d] = __uint_as_float(v[j]);
     };
-    bool ok = true;
     for (int i = 0; i < nq; ++i) {
-      if (__any_sync(0xffffffffu, *abort_flag != 0)) { ok = false; break; }
-      ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_DQFULL], i & 1));
-      if (!ok) break;
+      // leave together: the staging uses a named barrier over warps 4-7
+      bool stop = *abort_flag != 0;
+      if (!stop) stop = !mbar_wait(&bars[B_DQFULL], i & 1);
+      if (named_bar_any(2, 128, stop)) break;
       tc_fence_after();
-      const int q0 = i * kRows;
+      float* dst = dq_bh + (int64_t)q_tile_of(i, kv_tile, nq) * kRows * 128;
       uint32_t r0[32], r1[32];
       tmem_ld32(t_b + 0, r0);
       tmem_ld32(t_b + 32, r1);
       tmem_wait_ld();
-      reduce_chunk(r0, q0);
+      stage(stage_a, r0);
+      stage(stage_b, r1);
+      fence_proxy_async_smem();
+      named_bar_sync(2, 128);
+      if (leader) {
+        bulk_reduce_add_f32(dst, stage_a, 16384);
+        bulk_reduce_add_f32(dst + 32 * 128, stage_b, 16384);
+        bulk_commit_group();
+      }
+      // queries 64-127 into registers; then TMEM B can take dP^T_{i+1}
       tmem_ld32(t_b + 64, r0);
-      tmem_wait_ld();
-      reduce_chunk(r1, q0 + 32);
       tmem_ld32(t_b + 96, r1);
       tmem_wait_ld();
-      // every column of dQ^T_i is in registers: B can take dP^T_{i+1}
       tc_fence_before();
       mbar_arrive(&bars[B_DQFREE]);
-      reduce_chunk(r0, q0 + 64);
-      reduce_chunk(r1, q0 + 96);
+      if (leader) bulk_wait_group_read0();
+      named_bar_sync(2, 128);
+      stage(stage_a, r0);
+      stage(stage_b, r1);
+      fence_proxy_async_smem();
+      named_bar_sync(2, 128);
+      if (leader) {
+        bulk_reduce_add_f32(dst + 64 * 128, stage_a, 16384);
+        bulk_reduce_add_f32(dst + 96 * 128, stage_b, 16384);
+        bulk_commit_group();
+        bulk_wait_group_read0();
+        mbar_arrive(&bars[B_DSFREE]);
+      }
     }
-    if (!ok) *abort_flag = 1;
+    if (leader) bulk_wait_group0();  // reductions complete before exit
   }
 
   tc_fence_before();

@@ -7,7 +7,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "../../include/foundry_attn.h"
+#include "foundry_attn.h"
 
 namespace fa {
 
@@ -86,9 +86,11 @@ int launch_rope_pair(int dtype, const AttnShape& sh, const fa_tensor_t* x0,
                      const fa_tensor_t* y0, const fa_tensor_t* x1,
                      const fa_tensor_t* y1, const fa_rope_t* rope, int inverse,
                      int pos_offset, cudaStream_t stream, const float2* table);
+// x: fp32 (B, S, H, D) contiguous, or (B, H, s_pad, D) when s_pad > 0
 int launch_cast_f32(int dtype, const AttnShape& sh, const float* x,
                     const fa_tensor_t* y, float alpha, const fa_rope_t* rope,
-                    int pos_offset, cudaStream_t stream, const float2* table = nullptr);
+                    int pos_offset, cudaStream_t stream, const float2* table = nullptr,
+                    int s_pad = 0);
 int launch_lse_merge(int dtype, const AttnShape& sh, float* o_acc,
                      float* lse_acc, const fa_tensor_t* o_blk,
                      const float* lse_blk, int first, cudaStream_t stream);

@@ -10,7 +10,9 @@
 //
 // One CTA owns one 128-row Q tile of one (b, h) and streams 128-key K/V
 // tiles through TMA rings (K: 2 stages, V: 3 stages):
-//   warp 8      TMA producer (one lane)
+//   warp 8      TMA producer of Q and K (one lane)
+//   warp 10     TMA producer of V (one lane), so each ring fills as soon as
+//               its own stage frees
 //   warp 9      tcgen05 MMA issuer (one lane), TMEM owner
 //   warps 0-7   softmax, O rescale and epilogue: two warpgroups, each thread
 //               owns half a Q row (warpgroup 0 keys/columns 0-63, warpgroup 1
@@ -32,7 +34,7 @@ constexpr int kTileBytes = 32768;   // 128 x 128 bf16
 constexpr int kBlkBytes = 16384;    // one 64-column swizzle block
 constexpr int kKStages = 2;
 constexpr int kVStages = 3;
-constexpr int kThreads = 320;
+constexpr int kThreads = 352;
 
 // shared memory map (offsets from a 1024-byte aligned base)
 constexpr int kOffQ = 0;
@@ -118,41 +120,39 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 8) {
-    // ------------------------------------------------------------ producer
+    // --------------------------------------------------- producer: Q and K
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
-      tma_prefetch_desc(&tm_v);
       const int row = q_tile * kRows;
       mbar_arrive_expect_tx(&bars[B_Q], kTileBytes);
       tma_load_4d(smem + kOffQ, &tm_q, &bars[B_Q], 0, row, h, b);
       tma_load_4d(smem + kOffQ + kBlkBytes, &tm_q, &bars[B_Q], 64, row, h, b);
-      // K runs up to two tiles ahead of V (S(j+1) is computed before PV(j)).
-      int jk = 0, jv = 0;
       bool ok = true;
-      while (ok && (jk < nkv || jv < nkv)) {
+      for (int jk = 0; jk < nkv; ++jk) {
         if (*abort_flag) break;
-        if (jk < nkv && jk <= jv + 1) {
-          const int s = jk % kKStages, n = jk / kKStages;
-          if (jk >= kKStages) ok = mbar_wait(&bars[B_KEMPTY + s], (n - 1) & 1);
-          if (!ok) break;
-          uint8_t* d = smem + kOffK + s * kTileBytes;
-          mbar_arrive_expect_tx(&bars[B_KFULL + s], kTileBytes);
-          tma_load_4d(d, &tm_k, &bars[B_KFULL + s], 0, jk * kKeys, h, b);
-          tma_load_4d(d + kBlkBytes, &tm_k, &bars[B_KFULL + s], 64,
-                      jk * kKeys, h, b);
-          ++jk;
-        } else {
-          const int s = jv % kVStages, n = jv / kVStages;
-          if (jv >= kVStages) ok = mbar_wait(&bars[B_VEMPTY + s], (n - 1) & 1);
-          if (!ok) break;
-          uint8_t* d = smem + kOffV + s * kTileBytes;
-          mbar_arrive_expect_tx(&bars[B_VFULL + s], kTileBytes);
-          tma_load_4d(d, &tm_v, &bars[B_VFULL + s], 0, jv * kKeys, h, b);
-          tma_load_4d(d + kBlkBytes, &tm_v, &bars[B_VFULL + s], 64,
-                      jv * kKeys, h, b);
-          ++jv;
-        }
+        const int s = jk % kKStages, n = jk / kKStages;
+        if (jk >= kKStages && !(ok = mbar_wait(&bars[B_KEMPTY + s], (n - 1) & 1))) break;
+        uint8_t* d = smem + kOffK + s * kTileBytes;
+        mbar_arrive_expect_tx(&bars[B_KFULL + s], kTileBytes);
+        tma_load_4d(d, &tm_k, &bars[B_KFULL + s], 0, jk * kKeys, h, b);
+        tma_load_4d(d + kBlkBytes, &tm_k, &bars[B_KFULL + s], 64, jk * kKeys, h, b);
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else if (warp == 10) {
+    // ------------------------------------------------------- producer: V
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_v);
+      bool ok = true;
+      for (int jv = 0; jv < nkv; ++jv) {
+        if (*abort_flag) break;
+        const int s = jv % kVStages, n = jv / kVStages;
+        if (jv >= kVStages && !(ok = mbar_wait(&bars[B_VEMPTY + s], (n - 1) & 1))) break;
+        uint8_t* d = smem + kOffV + s * kTileBytes;
+        mbar_arrive_expect_tx(&bars[B_VFULL + s], kTileBytes);
+        tma_load_4d(d, &tm_v, &bars[B_VFULL + s], 0, jv * kKeys, h, b);
+        tma_load_4d(d + kBlkBytes, &tm_v, &bars[B_VFULL + s], 64, jv * kKeys, h, b);
       }
       if (!ok) *abort_flag = 1;
     }
@@ -237,9 +237,15 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
           for (int c = 0; c < 64; ++c)
             if (c >= valid) sv[c] = -INFINITY;
         }
-        mx = sv[0];
+        // pairwise tree: 6 dependent steps instead of a 63-long chain
+        float m32[32];
 #pragma unroll
-        for (int c = 1; c < 64; ++c) mx = fmaxf(mx, sv[c]);
+        for (int c = 0; c < 32; ++c) m32[c] = fmaxf(sv[c], sv[c + 32]);
+#pragma unroll
+        for (int w = 16; w >= 1; w >>= 1)
+#pragma unroll
+          for (int c = 0; c < w; ++c) m32[c] = fmaxf(m32[c], m32[c + w]);
+        mx = m32[0];
         red[((j & 1) * 2 + wg) * 128 + row_in_tile] = mx;
       }
       // both halves leave together; after this the partner's maximum is visible
@@ -256,16 +262,21 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
         m_use = m_cand;
         alpha = fast_exp2(m_run - m_cand);  // 0 when m_run == -inf
       }
-      float sum0 = 0.f, sum1 = 0.f;
+      // exponentials: every fourth on the FMA pipe (polynomial), the rest on
+      // MUFU; four partial sums keep the additions off one dependent chain
+      float sum4[4] = {0.f, 0.f, 0.f, 0.f};
       uint32_t pk[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        const float p0 = fast_exp2(fmaf(sv[2 * i], sl2, -m_use));
-        const float p1 = fast_exp2(fmaf(sv[2 * i + 1], sl2, -m_use));
-        sum0 += p0;
-        sum1 += p1;
+        const float x0 = fmaf(sv[2 * i], sl2, -m_use);
+        const float x1 = fmaf(sv[2 * i + 1], sl2, -m_use);
+        const float p0 = fast_exp2(x0);
+        const float p1 = (i & 1) ? exp2_poly(x1) : fast_exp2(x1);
+        sum4[(2 * i) & 3] += p0;
+        sum4[(2 * i + 1) & 3] += p1;
         pk[i] = pack_bf16(p0, p1);
       }
+      const float sum0 = sum4[0] + sum4[2], sum1 = sum4[1] + sum4[3];
       // P buffer j&1 is free once PV(j-2) has completed.
       if (j >= 2 && !__all_sync(0xffffffffu, mbar_wait(&bars[B_PVDONE + (j & 1)],
                                                         ((j - 2) >> 1) & 1))) {

@@ -312,7 +312,7 @@ size_t fa_bwd_workspace_bytes(int dtype, int B, int S, int H, int D,
     size_t total = rope_table_bytes(S, rope);
     if (rope) total += 2 * align256(n * 2);
     total += 2 * align256((size_t)B * H * s_pad * 4);
-    total += align256(n * 4);
+    total += align256((size_t)B * H * s_pad * D * 4);  // dq_acc (B, H, S_pad, D)
     return total;
   }
   size_t total = rope_table_bytes(S, rope);
@@ -365,14 +365,15 @@ int fa_bwd(int dtype, int B, int S, int H, int D, const fa_tensor_t* q,
     ws += align256((size_t)B * H * s_pad * 4);
     float* dq_acc = reinterpret_cast<float*>(ws);
     FA_TRY(launch_bwd_delta(dtype, sh, o, d_o, lse, delta, lse2, s_pad, st));
-    if (cudaMemsetAsync(dq_acc, 0, n * 4, st) != cudaSuccess) return FA_ERR_LAUNCH;
+    const size_t acc_bytes = (size_t)B * H * s_pad * D * 4;
+    FA_TRY(record_cuda_error(cudaMemsetAsync(dq_acc, 0, acc_bytes, st)));
     cudaEvent_t stop = timer_begin(FA_TIMER_BWD, st);
     const int rc = launch_attn_bwd_bf16(sh, S, &qr, &kr, v, d_o, lse2, delta,
                                         dq_acc, dk, dv, nullptr, nullptr, scale,
                                         rope, table, st);
     timer_end(stop, st);
     FA_TRY(rc);
-    return launch_cast_f32(dtype, sh, dq_acc, dq, scale, rope, 0, st, table);
+    return launch_cast_f32(dtype, sh, dq_acc, dq, scale, rope, 0, st, table, s_pad);
   }
   // fp32 path
   fa_tensor_t dqr = *dq, dkr = *dk;

@@ -259,11 +259,15 @@ int launch_rope_pair(int dtype, const AttnShape& sh, const fa_tensor_t* x0,
 
 int launch_cast_f32(int dtype, const AttnShape& sh, const float* x,
                     const fa_tensor_t* y, float alpha, const fa_rope_t* rope,
-                    int pos_offset, cudaStream_t stream, const float2* table) {
+                    int pos_offset, cudaStream_t stream, const float2* table,
+                    int s_pad) {
   RopeArgs r = make_rope_args(rope, dtype == FA_DTYPE_BF16 ? 1 : 0, pos_offset);
   r.table = table;
   const int64_t D = sh.D;
-  misc::TView xv{x, (int64_t)sh.S * sh.H * D, (int64_t)sh.H * D, D};
+  // x is (B, S, H, D) contiguous, or (B, H, s_pad, D) when s_pad > 0
+  const misc::TView xv =
+      s_pad > 0 ? misc::TView{x, (int64_t)sh.H * s_pad * D, D, (int64_t)s_pad * D}
+                : misc::TView{x, (int64_t)sh.S * sh.H * D, (int64_t)sh.H * D, D};
   return launch_rope_generic(FA_DTYPE_F32, dtype, sh, xv, misc::tout(y), r,
                              alpha, 1, stream);
 }

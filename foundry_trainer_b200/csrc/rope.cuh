@@ -13,7 +13,7 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
-#include "../../include/foundry_attn.h"
+#include "foundry_attn.h"
 
 namespace fa {
 
