@@ -341,11 +341,6 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
       // which chunk c or an earlier chunk has already read.
       uint32_t s_hi[32];
       tmem_ld32(t_a + 32, s_hi);
-      // the drain of dQ_{i-1} must have released the shared dS^T tile
-      if (i > 0) {
-        ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_DSFREE], (i - 1) & 1));
-        if (!ok) break;
-      }
 #pragma unroll
       for (int cb = 0; cb < 4; ++cb) {
         uint32_t dr[16], s_lo[16];
@@ -373,16 +368,24 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
         }
         tmem_st8(t_a + cb * 8, pk);       // P^T: columns 64h + [0, 32)
         tmem_st8(t_a + 32 + cb * 8, dk);  // dS^T: columns 64h + [32, 64)
-        // dS^T row -> shared memory: queries 64h + [16cb, 16cb+16) are
-        // 16-byte chunks 2cb, 2cb+1 of swizzle block h.
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const uint32_t off = sw128_offset(key_in_tile, cb * 2 + u);
-          *reinterpret_cast<uint4*>(ds_blk + off) =
-              make_uint4(dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
-        }
       }
       tmem_wait_st();
+      // dS^T also goes to shared memory (B operand of dQ^T), once the drain
+      // of dQ_{i-1} has released the tile: read back this half's 32 packed
+      // columns and store them as 16-byte chunks 0-7 of swizzle block h.
+      if (i > 0) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_DSFREE], (i - 1) & 1));
+        if (!ok) break;
+      }
+      {
+        uint32_t dsr[32];
+        tmem_ld32(t_a + 32, dsr);
+        tmem_wait_ld();
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          *reinterpret_cast<uint4*>(ds_blk + sw128_offset(key_in_tile, u)) =
+              make_uint4(dsr[4 * u], dsr[4 * u + 1], dsr[4 * u + 2], dsr[4 * u + 3]);
+      }
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&bars[B_PS]);

@@ -9,7 +9,9 @@
 // end (both are one bf16 rounding of P; the LSE itself is fp32).
 //
 // One CTA owns one 128-row Q tile of one (b, h) and streams 128-key K/V
-// tiles through TMA rings (K: 2 stages, V: 3 stages):
+// tiles through TMA rings (K: 2 stages, V: 3 stages), starting at K/V tile
+// `q_tile` and wrapping, so the CTAs of one head do not all request the same
+// tile from L2 at once (the online softmax is order-independent):
 //   warp 8      TMA producer of Q and K (one lane)
 //   warp 10     TMA producer of V (one lane), so each ring fills as soon as
 //               its own stage frees
@@ -62,6 +64,12 @@ constexpr int B_FINAL = 17;
 constexpr uint32_t kColS = 0;
 constexpr uint32_t kColP = 256;  // + 64 * (j & 1)
 constexpr uint32_t kColO = 384;
+
+// K/V tile visited at step j by the CTA of Q tile `q_tile`.
+__device__ __forceinline__ int kv_tile_of(int j, int q_tile, int nkv) {
+  const int t = j + q_tile % nkv;
+  return t >= nkv ? t - nkv : t;
+}
 
 struct Params {
   int S, H, nkv;
@@ -135,8 +143,9 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
         if (jk >= kKStages && !(ok = mbar_wait(&bars[B_KEMPTY + s], (n - 1) & 1))) break;
         uint8_t* d = smem + kOffK + s * kTileBytes;
         mbar_arrive_expect_tx(&bars[B_KFULL + s], kTileBytes);
-        tma_load_4d(d, &tm_k, &bars[B_KFULL + s], 0, jk * kKeys, h, b);
-        tma_load_4d(d + kBlkBytes, &tm_k, &bars[B_KFULL + s], 64, jk * kKeys, h, b);
+        const int krow = kv_tile_of(jk, q_tile, nkv) * kKeys;
+        tma_load_4d(d, &tm_k, &bars[B_KFULL + s], 0, krow, h, b);
+        tma_load_4d(d + kBlkBytes, &tm_k, &bars[B_KFULL + s], 64, krow, h, b);
       }
       if (!ok) *abort_flag = 1;
     }
@@ -151,8 +160,9 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
         if (jv >= kVStages && !(ok = mbar_wait(&bars[B_VEMPTY + s], (n - 1) & 1))) break;
         uint8_t* d = smem + kOffV + s * kTileBytes;
         mbar_arrive_expect_tx(&bars[B_VFULL + s], kTileBytes);
-        tma_load_4d(d, &tm_v, &bars[B_VFULL + s], 0, jv * kKeys, h, b);
-        tma_load_4d(d + kBlkBytes, &tm_v, &bars[B_VFULL + s], 64, jv * kKeys, h, b);
+        const int vrow = kv_tile_of(jv, q_tile, nkv) * kKeys;
+        tma_load_4d(d, &tm_v, &bars[B_VFULL + s], 0, vrow, h, b);
+        tma_load_4d(d + kBlkBytes, &tm_v, &bars[B_VFULL + s], 64, vrow, h, b);
       }
       if (!ok) *abort_flag = 1;
     }
@@ -231,7 +241,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
         tmem_ld32(t_s + 32, sr + 32);
         tmem_wait_ld();
         float* sv = reinterpret_cast<float*>(sr);
-        const int valid = p.S - j * kKeys - wg * 64;
+        const int valid = p.S - kv_tile_of(j, q_tile, nkv) * kKeys - wg * 64;
         if (valid < 64) {
 #pragma unroll
           for (int c = 0; c < 64; ++c)
