@@ -118,6 +118,103 @@ __global__ void rope_table_kernel(RopeArgs r, int S, float2* table) {
   table[(int64_t)(t + r.pos_offset) * nf + f] = rope_cs(direct, t, f);
 }
 
+// ------------------------------------------------ token-major fast paths
+// For the reference layout (head_dim 128 = four 32-wide axes) with a (cos,
+// sin) table: one block per token, one warp per head row; lane l owns
+// elements 4l..4l+3 (one 8- or 16-byte access per lane, a whole row per warp
+// instruction); the rotate-half partner of element 4l+u is element 4(l^4)+u.
+template <typename T>
+struct Vec4;
+template <>
+struct Vec4<float> {
+  static __device__ __forceinline__ void load(const float* p, float* v) {
+    const float4 x = *reinterpret_cast<const float4*>(p);
+    v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+  }
+  static __device__ __forceinline__ void store(float* p, const float* v) {
+    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  }
+};
+template <>
+struct Vec4<__nv_bfloat16> {
+  static __device__ __forceinline__ void load(const __nv_bfloat16* p, float* v) {
+    const uint2 x = *reinterpret_cast<const uint2*>(p);
+    v[0] = __uint_as_float(x.x << 16); v[1] = __uint_as_float(x.x & 0xFFFF0000u);
+    v[2] = __uint_as_float(x.y << 16); v[3] = __uint_as_float(x.y & 0xFFFF0000u);
+  }
+  static __device__ __forceinline__ void store(__nv_bfloat16* p, const float* v) {
+    *reinterpret_cast<uint2*>(p) = make_uint2(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]));
+  }
+};
+
+// y = alpha * rot(x) (or the inverse rotation); blockIdx.x = token (b, s),
+// blockIdx.y selects the (x, y) pair.
+template <typename Tin, typename Tout>
+__global__ void rope_token_kernel(TView x0, TOut y0, TView x1, TOut y1,
+                                  RopeArgs r, int S, int H, float alpha,
+                                  int inverse) {
+  const TView& x = blockIdx.y == 0 ? x0 : x1;
+  const TOut& y = blockIdx.y == 0 ? y0 : y1;
+  const int s = (int)(blockIdx.x % S), b = (int)(blockIdx.x / S);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float c[4], sn[4];
+  const bool rotate = r.pos != nullptr;
+  const bool first = (lane & 7) < 4;  // element in the first half of its axis
+  if (rotate) {
+    const float4* tab = reinterpret_cast<const float4*>(
+        r.table + (int64_t)(s + r.pos_offset) * 64 + (lane >> 3) * 16 + (lane & 3) * 4);
+    const float4 t0 = tab[0], t1 = tab[1];
+    c[0] = t0.x; sn[0] = t0.y; c[1] = t0.z; sn[1] = t0.w;
+    c[2] = t1.x; sn[2] = t1.y; c[3] = t1.z; sn[3] = t1.w;
+  }
+  // forward: first half y = x c - x' s, second half y = x c + x' s;
+  // inverse: the transposed rotation (signs swapped)
+  const float sgn = (first != (inverse != 0)) ? -1.f : 1.f;
+  for (int h = warp; h < H; h += blockDim.x >> 5) {
+    const Tin* px = reinterpret_cast<const Tin*>(x.p) + b * x.sb + s * x.ss + h * x.sh + 4 * lane;
+    Tout* py = reinterpret_cast<Tout*>(y.p) + b * y.sb + s * y.ss + h * y.sh + 4 * lane;
+    float v[4];
+    Vec4<Tin>::load(px, v);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) v[u] *= alpha;
+    if (rotate) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float other = __shfl_xor_sync(0xffffffffu, v[u], 4);
+        v[u] = __fadd_rn(__fmul_rn(v[u], c[u]), __fmul_rn(sgn * other, sn[u]));
+      }
+    }
+    Vec4<Tout>::store(py, v);
+  }
+}
+
+// delta[b, h, s] = sum_d dO * O over s < s_pad (0 past S); lse2 likewise
+// (+inf past S). One block per token (b, s), one warp per head.
+template <typename T>
+__global__ void delta_token_kernel(TView o, TView d_o, const float* lse,
+                                   float* delta, float* lse2, int S, int H,
+                                   int s_pad) {
+  const int s = (int)(blockIdx.x % s_pad), b = (int)(blockIdx.x / s_pad);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int h = warp; h < H; h += blockDim.x >> 5) {
+    float acc = 0.f;
+    if (s < S) {
+      float a[4], g[4];
+      Vec4<T>::load(reinterpret_cast<const T*>(o.p) + b * o.sb + s * o.ss + h * o.sh + 4 * lane, a);
+      Vec4<T>::load(reinterpret_cast<const T*>(d_o.p) + b * d_o.sb + s * d_o.ss + h * d_o.sh + 4 * lane, g);
+      acc = a[0] * g[0] + a[1] * g[1] + a[2] * g[2] + a[3] * g[3];
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (lane == 0) {
+      const int64_t bh = (int64_t)b * H + h;
+      delta[bh * s_pad + s] = acc;
+      if (lse2 != nullptr)
+        lse2[bh * s_pad + s] = (s < S) ? lse[bh * S + s] * 1.4426950408889634f : INFINITY;
+    }
+  }
+}
+
 // Generic thread-per-row rotation for other axis layouts.
 template <typename Tin, typename Tout>
 __global__ void rope_row_kernel(TView x, TOut y, RopeArgs r, int S, int H,
@@ -174,9 +271,29 @@ TOut tout(const fa_tensor_t* t) { return TOut{t->data, t->stride_b, t->stride_s,
 
 }  // namespace misc
 
+// 4-element vector accesses need rows aligned to 4 elements and strides that
+// are multiples of 4 elements
+template <typename V>
+static bool aligned16(const V& t, int dtype) {
+  const int64_t es = dtype == FA_DTYPE_BF16 ? 2 : 4;
+  return (reinterpret_cast<uintptr_t>(t.p) % (4 * es)) == 0 && t.sb % 4 == 0 &&
+         t.ss % 4 == 0 && t.sh % 4 == 0;
+}
+
 int launch_bwd_delta(int dtype, const AttnShape& sh, const fa_tensor_t* o,
                      const fa_tensor_t* d_o, const float* lse, float* delta,
                      float* lse2, int s_pad, cudaStream_t stream) {
+  const misc::TView ov = misc::tview(o), dv = misc::tview(d_o);
+  if (sh.D == 128 && aligned16(ov, dtype) && aligned16(dv, dtype)) {
+    const dim3 grid((unsigned)((int64_t)sh.B * s_pad));
+    if (dtype == FA_DTYPE_BF16)
+      misc::delta_token_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
+          ov, dv, lse, delta, lse2, sh.S, sh.H, s_pad);
+    else
+      misc::delta_token_kernel<float><<<grid, 256, 0, stream>>>(
+          ov, dv, lse, delta, lse2, sh.S, sh.H, s_pad);
+    return launch_status();
+  }
   const int64_t rows = (int64_t)sh.B * sh.H * s_pad;
   const dim3 grid((unsigned)((rows + misc::kWarps - 1) / misc::kWarps));
   if (dtype == FA_DTYPE_BF16)
@@ -198,6 +315,22 @@ static int launch_rope_generic(int dtype_in, int dtype_out, const AttnShape& sh,
   const misc::TView x2 = xb != nullptr ? *xb : x;
   const misc::TOut y2 = yb != nullptr ? *yb : y;
   const int64_t rows = (int64_t)sh.B * sh.S * sh.H;
+  const bool token_path =
+      sh.D == 128 && (r.pos == nullptr || (r.axis_dim == 32 && r.n_axes == 4 && r.table != nullptr)) &&
+      aligned16(x, dtype_in) && aligned16(y, dtype_out) && aligned16(x2, dtype_in) &&
+      aligned16(y2, dtype_out);
+  if (token_path) {
+    const dim3 grid((unsigned)((int64_t)sh.B * sh.S), npairs);
+#define FA_ROPE_T(TI, TO)                                                    \
+  misc::rope_token_kernel<TI, TO><<<grid, 256, 0, stream>>>(x, y, x2, y2, r, sh.S, \
+                                                           sh.H, alpha, inverse)
+    if (dtype_in == FA_DTYPE_BF16 && dtype_out == FA_DTYPE_BF16) FA_ROPE_T(__nv_bfloat16, __nv_bfloat16);
+    else if (dtype_in == FA_DTYPE_F32 && dtype_out == FA_DTYPE_BF16) FA_ROPE_T(float, __nv_bfloat16);
+    else if (dtype_in == FA_DTYPE_F32 && dtype_out == FA_DTYPE_F32) FA_ROPE_T(float, float);
+    else FA_ROPE_T(__nv_bfloat16, float);
+#undef FA_ROPE_T
+    return launch_status();
+  }
   const bool warp_path = (r.pos == nullptr) || (r.axis_dim == 32 && r.n_axes <= 4);
   if (warp_path) {
     const dim3 grid((unsigned)((rows + misc::kWarps - 1) / misc::kWarps));
