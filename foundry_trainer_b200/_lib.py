@@ -70,6 +70,8 @@ SIGNATURES = {
                                  _T, _F, _F, _F, _F, _F, C.c_float, C.c_void_p]),
     "fa_cast_f32": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _F, _T, C.c_float, _R,
                               C.c_void_p]),
+    "fa_bwd_noalloc": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, _T, _T, _T, _T, _T, _F, _T, _T,
+                                 _T, C.c_float, C.c_void_p]),
     "fa_timing_enable": (C.c_int, [C.c_int]),
     "fa_timing_read": (C.c_int, [C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_int)]),
     "fa_status_string": (C.c_char_p, [C.c_int]),

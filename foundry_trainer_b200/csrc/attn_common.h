@@ -38,6 +38,8 @@ enum KernelId {
 // FA_ERR_LAUNCH.
 int launch_status();
 int record_cuda_error(cudaError_t e);
+// Sets the text fa_last_error() returns on this thread.
+void record_error_text(const char* msg);
 
 // Raises the dynamic shared-memory limit of `fn` once per (device, kernel).
 int ensure_smem_attr(const void* fn, int bytes, int kernel_id);

@@ -85,6 +85,10 @@ int record_cuda_error(cudaError_t e) {
 
 int launch_status() { return record_cuda_error(cudaGetLastError()); }
 
+void record_error_text(const char* msg) {
+  std::snprintf(g_last_error, sizeof(g_last_error), "%s", msg);
+}
+
 // ------------------------------------------------- per-device attributes
 static std::atomic<int> g_attr_done[64][kKernelCount];
 

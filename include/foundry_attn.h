@@ -162,6 +162,34 @@ int fa_cast_f32(int dtype, int B, int S, int H, int D, const float* x,
                 void* stream);
 
 /*
+ * Backward without a caller workspace. This entry point has no counterpart in
+ * the reference. It is for callers that cannot allocate device memory where
+ * they call the op: a host framework whose memory pool already owns the GPU
+ * and offers no raw allocation here, or a path on which cudaMalloc's implicit
+ * device-wide synchronisation is not acceptable. It computes what fa_bwd
+ * computes for dtype FA_DTYPE_BF16 without RoPE and non-deterministic dQ
+ * summation, taking its scratch (the fp32 dQ accumulator and two per-row
+ * tables) from a 64 MiB array built into the library instead of a workspace;
+ * it allocates nothing. Limits and rules:
+ *   - B * H * ceil(S/128) * 128 rows must fit the 64 MiB array (about 129k
+ *     rows, e.g. B=1, H=24, S <= 5376); larger sizes return FA_ERR_TOO_LARGE
+ *     and fa_last_error() says why.
+ *   - The array exists once per GPU that loads the library and stays resident
+ *     until the process exits.
+ *   - The first call on a device looks up the array's device address (with
+ *     that device current); make that first call before any stream capture.
+ *   - All calls on one device share the array: calls whose GPU work overlaps
+ *     (streams without ordering between them) race and corrupt each other's
+ *     dQ. The accumulator is cleared at the start of every call.
+ */
+int fa_bwd_noalloc(int B, int S, int H, int D, const fa_tensor_t* q,
+                   const fa_tensor_t* k, const fa_tensor_t* v,
+                   const fa_tensor_t* o, const fa_tensor_t* d_o,
+                   const float* lse, const fa_tensor_t* dq,
+                   const fa_tensor_t* dk, const fa_tensor_t* dv, float scale,
+                   void* stream);
+
+/*
  * Measurement hooks (no counterpart in the reference, which only wall-clocks
  * whole steps, bin/throughput.rs:868-873). While enabled, every launch of the
  * main forward (FA_TIMER_FWD) and backward (FA_TIMER_BWD) kernel is bracketed
