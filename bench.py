@@ -220,19 +220,43 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
 
-    # weak scaling: each rank owns one batch x head partition of cfg's size
-    q, k, v, d_o = (t.to(dev) for t in configs.make_inputs(cfg))
-    pos = configs.positions(cfg.txt, cfg.grid).to(dev)
-    rope = ops.Rope(pos)
-    o = torch.empty_like(q)
-    lse = torch.empty((cfg.B, cfg.H, cfg.S), device=dev, dtype=torch.float32)
-    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    ring_mode = cfg.name == "c5"
+    pos_full = configs.positions(cfg.txt, cfg.grid)
+    if ring_mode:
+        # strong scaling: one sequence sharded along S over the ranks, K/V
+        # (and dK/dV accumulators) passed round a ring over NCCL
+        from foundry_trainer_b200 import ring
+        if cfg.S % world != 0:
+            raise SystemExit(f"{cfg.name}: S={cfg.S} does not split over {world} ranks")
+        n_loc = cfg.S // world
+        sl = slice(rank * n_loc, (rank + 1) * n_loc)
+        q, k, v, d_o = (t[:, sl].contiguous().to(dev) for t in configs.make_inputs(cfg))
+        pos = pos_full[sl].contiguous().to(dev)
+        comm, kern = ring.RingComm(), ring.RingKernels()
+        scale = ops.default_scale(cfg.D)
+        outs = {}
+
+        def step():
+            o_, lse_, q_r, k_r = ring.ring_fwd(q, k, v, pos, scale, comm, kern)
+            outs["o"] = o_
+            outs["dq"], outs["dk"], outs["dv"] = ring.ring_bwd(q_r, k_r, v, o_, d_o, lse_, pos,
+                                                                scale, comm, kern)
+    else:
+        # weak scaling: each rank owns one batch x head partition of cfg's size
+        n_loc = cfg.S
+        q, k, v, d_o = (t.to(dev) for t in configs.make_inputs(cfg))
+        pos = pos_full.to(dev)
+        rope = ops.Rope(pos)
+        o = torch.empty_like(q)
+        lse = torch.empty((cfg.B, cfg.H, cfg.S), device=dev, dtype=torch.float32)
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        outs = {"o": o, "dq": dq, "dk": dk, "dv": dv}
+
+        def step():
+            ops.attn_fwd(q, k, v, rope=rope, out=o, lse=lse)
+            ops.attn_bwd(q, k, v, o, d_o, lse, rope=rope, dq=dq, dk=dk, dv=dv)
     flush_buf = torch.empty(256 * 1024 * 1024 // 4, device=dev, dtype=torch.float32)
     lib = _lib.load()
-
-    def step():
-        ops.attn_fwd(q, k, v, rope=rope, out=o, lse=lse)
-        ops.attn_bwd(q, k, v, o, d_o, lse, rope=rope, dq=dq, dk=dk, dv=dv)
 
     sampler = ClockSampler(local)
     sampler.start()  # started early so samples exist under load near the timed region
@@ -244,10 +268,15 @@ def main():
     # The timed step replays a CUDA graph of the same public-API calls, so
     # host-side launch overhead (ctypes, descriptor encoding) is not timed as
     # device idle; per-kernel times come from an eager pass with the event hooks.
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        step()
-    graph.replay()
+    # The ring step holds NCCL exchanges and runs eagerly.
+    if ring_mode:
+        run = step
+    else:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        run = graph.replay
+    run()
     torch.cuda.synchronize()
 
     K = args.steps
@@ -257,7 +286,7 @@ def main():
     # sampler sees the load); these replays are not timed
     t_end = time.time() + 0.5
     while time.time() < t_end:
-        graph.replay()
+        run()
         torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -267,7 +296,7 @@ def main():
     for i in range(K):
         flush_buf.zero_()  # L2 (126 MB) flushed between timed steps, outside the events
         starts[i].record()
-        graph.replay()
+        run()
         ends[i].record()
     torch.cuda.synchronize()
     wall = time.perf_counter() - wall0
@@ -298,14 +327,18 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     step_ms_max, bwd_ms, fwd_ms = t.tolist()
 
-    flops_step = cfg.flops_fwd_bwd()
-    value = world * K * flops_step / (step_ms_max / 1e3) / 1e12
+    # whole-job FLOPs per step: every rank's own problem (weak), or the one
+    # sharded sequence (ring, strong)
+    flops_step = cfg.flops_fwd_bwd() * (1 if ring_mode else world)
+    value = K * flops_step / (step_ms_max / 1e3) / 1e12
+    # per kernel launch: the whole local problem, or one ring block
+    blk = 4.0 * cfg.B * cfg.H * n_loc * n_loc * cfg.D
 
     peaks = _peaks()
     timed_seconds = step_ms_max / 1e3
     peak_kind = "bf16_sustained" if timed_seconds > 2.0 else "bf16"
     peak = peaks[peak_kind]
-    bwd_flops = cfg.flops_bwd()
+    bwd_flops = 2.5 * blk
     achieved = bwd_flops / (bwd_ms / 1e3) / 1e12
     traffic = None
     tf = ROOT / "profiles" / "traffic.json"
@@ -317,7 +350,7 @@ def main():
     roofline = {"kernel": "attn_bwd_kernel", "bound": "tensor", "achieved": achieved,
                 "peak": peak, "unit": UNIT, "frac": achieved / peak, "traffic": traffic,
                 "peak_source": f"{peaks['source']} {peak_kind}",
-                "fwd_kernel": {"achieved": cfg.flops_fwd() / (fwd_ms / 1e3) / 1e12,
+                "fwd_kernel": {"achieved": blk / (fwd_ms / 1e3) / 1e12,
                                "ms": fwd_ms},
                 "bwd_kernel_ms": bwd_ms,
                 "flops_per_launch": bwd_flops}
@@ -326,7 +359,8 @@ def main():
     e2e = None
     if not args.no_e2e:
         hq, hk, hv, hdo = (x.cpu().pin_memory() for x in (q, k, v, d_o))
-        ho, hdq, hdk, hdv = (torch.empty_like(x, device="cpu").pin_memory() for x in (o, dq, dk, dv))
+        ho, hdq, hdk, hdv = (torch.empty_like(outs[n], device="cpu").pin_memory()
+                             for n in ("o", "dq", "dk", "dv"))
         h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv, hdo))
         d2h = sum(x.numel() * x.element_size() for x in (ho, hdq, hdk, hdv))
 
@@ -336,10 +370,10 @@ def main():
             v.copy_(hv, non_blocking=True)
             d_o.copy_(hdo, non_blocking=True)
             step()
-            ho.copy_(o, non_blocking=True)
-            hdq.copy_(dq, non_blocking=True)
-            hdk.copy_(dk, non_blocking=True)
-            hdv.copy_(dv, non_blocking=True)
+            ho.copy_(outs["o"], non_blocking=True)
+            hdq.copy_(outs["dq"], non_blocking=True)
+            hdk.copy_(outs["dk"], non_blocking=True)
+            hdv.copy_(outs["dv"], non_blocking=True)
 
         for _ in range(args.warmup):
             e2e_step()
@@ -355,11 +389,13 @@ def main():
         te = torch.tensor([s0.elapsed_time(s1)], device=dev, dtype=torch.float64)
         if world > 1:
             dist.all_reduce(te, op=dist.ReduceOp.MAX)
-        e2e = {"value": world * K * flops_step / (te.item() / 1e3) / 1e12, "unit": UNIT,
+        e2e = {"value": K * flops_step / (te.item() / 1e3) / 1e12, "unit": UNIT,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "ms_per_step": te.item() / K,
-               "path": "ops.attn_fwd + ops.attn_bwd (C ABI fa_fwd/fa_bwd) with pinned host "
-                       "q,k,v,dO in and o,dq,dk,dv out each step"}
+               "path": ("ring.ring_fwd + ring.ring_bwd (C ABI fa_fwd_partial/fa_bwd_partial "
+                        "round an NCCL ring)" if ring_mode else
+                        "ops.attn_fwd + ops.attn_bwd (C ABI fa_fwd/fa_bwd)") +
+                       " with pinned host q,k,v,dO in and o,dq,dk,dv out each step, per rank"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -373,18 +409,29 @@ def main():
         dist.destroy_process_group()
     if rank != 0:
         return
-    launches_per_step = 8  # rope q,k + fwd; rope q,k + delta + bwd + dQ cast
+    if ring_mode:
+        # fwd: rope q, rope k, W blocks + W merges, O cast; bwd: prepare,
+        # W blocks, W-1 accumulator adds, 3 casts
+        launches_per_step = 4 * world + 6
+        workload = (f"{cfg.name}: B={cfg.B} H={cfg.H} S={cfg.S} ({cfg.txt} text + "
+                    f"{cfg.grid}x{cfg.grid} image) D={cfg.D}, one sequence sharded "
+                    f"{n_loc} rows per rank, non-causal, axial RoPE")
+        parallelism = f"sequence ring x{world} (NCCL send/recv of K,V and fp32 dK,dV)"
+    else:
+        launches_per_step = 8  # rope q,k + fwd; rope q,k + delta + bwd + dQ cast
+        workload = (f"{cfg.name}: B={cfg.B} H={cfg.H} S={cfg.S} "
+                    f"({cfg.txt} text + {cfg.grid}x{cfg.grid} image) D={cfg.D} "
+                    f"per rank, non-causal, axial RoPE inside the op")
+        parallelism = f"batch-sharded x{world}, no collective on the data path"
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": args.warmup, "ms_per_step": step_ms_max / K, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "scaling": "strong" if ring_mode else "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded torch.Generator, q,k,v ~ 0.5*N(0,1), dO ~ N(0,1))",
-        "config": {"workload": f"{cfg.name}: B={cfg.B} H={cfg.H} S={cfg.S} "
-                               f"({cfg.txt} text + {cfg.grid}x{cfg.grid} image) D={cfg.D} "
-                               f"per rank, non-causal, axial RoPE inside the op",
-                   "per_rank_B": cfg.B, "H": cfg.H, "S": cfg.S, "D": cfg.D,
+        "config": {"workload": workload,
+                   "per_rank_B": cfg.B, "H": cfg.H, "S": cfg.S, "S_per_rank": n_loc, "D": cfg.D,
                    "l2": "flushed between timed steps (256 MB write outside the step events)",
-                   "parallelism": f"batch-sharded x{world}, no collective on the data path"},
+                   "parallelism": parallelism},
         "roofline": roofline,
         "cpu_baseline": cpu,
         "e2e": e2e,

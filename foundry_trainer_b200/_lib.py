@@ -64,12 +64,13 @@ SIGNATURES = {
                                  _T, _F, C.c_float, C.c_void_p]),
     "fa_lse_merge": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _F, _F, _T, _F,
                                C.c_int, C.c_void_p]),
-    "fa_bwd_delta": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _T, _T, _F,
-                               C.c_void_p]),
+    "fa_bwd_prepare": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _T, _T, _F, _F, _F,
+                                 C.c_void_p]),
     "fa_bwd_partial": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _T, _T, _T,
-                                 _T, _F, _F, _F, _F, _F, C.c_float, C.c_void_p]),
-    "fa_cast_f32": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _F, _T, C.c_float, _R,
-                              C.c_void_p]),
+                                 _T, _F, _F, _F, _F, _F, C.c_int, C.c_float, C.c_void_p]),
+    "fa_add_f32": (C.c_int, [C.c_int64, _F, _F, C.c_void_p]),
+    "fa_cast_f32": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _F, C.c_int, _T,
+                              C.c_float, _R, C.c_void_p]),
     "fa_bwd_noalloc": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, _T, _T, _T, _T, _T, _F, _T, _T,
                                  _T, C.c_float, C.c_void_p]),
     "fa_timing_enable": (C.c_int, [C.c_int]),

@@ -78,7 +78,8 @@ struct Params {
   float scale, scale_log2;
   const float* lse2_pad;    // (B, H, s_pad): LSE * log2(e), +inf padding
   const float* delta_pad;   // (B, H, s_pad): rowsum(dO*O), 0 padding
-  // dK / dV output: bf16 strided tensors, or fp32 accumulators when acc != 0
+  // dK / dV output: bf16 strided tensors (acc 0), or fp32 (B, kv_len, H, D)
+  // buffers that the result is added to (acc 1) or stored in (acc 2)
   int acc;
   __nv_bfloat16* dk;
   int64_t dks_b, dks_s, dks_h;
@@ -125,11 +126,14 @@ __device__ __forceinline__ void store_half_row(const Params& p, bool is_dk,
     float4* d4 = reinterpret_cast<float4*>(dst);
 #pragma unroll
     for (int c = 0; c < 16; ++c) {
-      float4 o = d4[c];
-      o.x += v[4 * c + 0];
-      o.y += v[4 * c + 1];
-      o.z += v[4 * c + 2];
-      o.w += v[4 * c + 3];
+      float4 o = make_float4(v[4 * c + 0], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+      if (p.acc == 1) {
+        const float4 a = d4[c];
+        o.x += a.x;
+        o.y += a.y;
+        o.z += a.z;
+        o.w += a.w;
+      }
       d4[c] = o;
     }
   } else {
@@ -491,7 +495,7 @@ int launch_attn_bwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
                          const fa_tensor_t* d_o, const float* lse2_pad,
                          const float* delta_pad, float* dq_acc,
                          const fa_tensor_t* dk, const fa_tensor_t* dv,
-                         float* dk_acc, float* dv_acc, float scale,
+                         float* dk_acc, float* dv_acc, int accumulate, float scale,
                          const fa_rope_t* rope, const float2* rope_table,
                          cudaStream_t stream) {
   if (rope != nullptr && (rope->axis_dim != 32 || rope->n_axes != 4))
@@ -512,7 +516,7 @@ int launch_attn_bwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
   p.scale_log2 = scale * 1.4426950408889634f;
   p.lse2_pad = lse2_pad;
   p.delta_pad = delta_pad;
-  p.acc = (dk_acc != nullptr) ? 1 : 0;
+  p.acc = (dk_acc != nullptr) ? (accumulate ? 1 : 2) : 0;
   p.dk = dk ? reinterpret_cast<__nv_bfloat16*>(dk->data) : nullptr;
   p.dks_b = dk ? dk->stride_b : 0;
   p.dks_s = dk ? dk->stride_s : 0;

@@ -45,7 +45,7 @@ void record_error_text(const char* msg);
 int ensure_smem_attr(const void* fn, int bytes, int kernel_id);
 
 // bf16 sm_100a kernels
-int launch_attn_fwd_bf16(const AttnShape& sh, const fa_tensor_t* q,
+int launch_attn_fwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
                          const fa_tensor_t* k, const fa_tensor_t* v,
                          const fa_tensor_t* o, float* lse, float scale,
                          cudaStream_t stream);
@@ -55,7 +55,7 @@ int launch_attn_bwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
                          const fa_tensor_t* d_o, const float* lse2_pad,
                          const float* delta_pad, float* dq_acc,
                          const fa_tensor_t* dk, const fa_tensor_t* dv,
-                         float* dk_acc, float* dv_acc, float scale,
+                         float* dk_acc, float* dv_acc, int accumulate, float scale,
                          const fa_rope_t* rope, const float2* rope_table,
                          cudaStream_t stream);
 
@@ -93,6 +93,8 @@ int launch_cast_f32(int dtype, const AttnShape& sh, const float* x,
                     const fa_tensor_t* y, float alpha, const fa_rope_t* rope,
                     int pos_offset, cudaStream_t stream, const float2* table = nullptr,
                     int s_pad = 0);
+// dst[i] += src[i], i < n
+int launch_add_f32(int64_t n, float* dst, const float* src, cudaStream_t stream);
 int launch_lse_merge(int dtype, const AttnShape& sh, float* o_acc,
                      float* lse_acc, const fa_tensor_t* o_blk,
                      const float* lse_blk, int first, cudaStream_t stream);

@@ -72,7 +72,7 @@ __device__ __forceinline__ int kv_tile_of(int j, int q_tile, int nkv) {
 }
 
 struct Params {
-  int S, H, nkv;
+  int S, H, kv_len, nkv;
   float scale_log2;  // scale * log2(e)
   __nv_bfloat16* o;
   int64_t os_b, os_s, os_h;
@@ -241,7 +241,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
         tmem_ld32(t_s + 32, sr + 32);
         tmem_wait_ld();
         float* sv = reinterpret_cast<float*>(sr);
-        const int valid = p.S - kv_tile_of(j, q_tile, nkv) * kKeys - wg * 64;
+        const int valid = p.kv_len - kv_tile_of(j, q_tile, nkv) * kKeys - wg * 64;
         if (valid < 64) {
 #pragma unroll
           for (int c = 0; c < 64; ++c)
@@ -375,21 +375,22 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
 
 }  // namespace fwd
 
-int launch_attn_fwd_bf16(const AttnShape& sh, const fa_tensor_t* q,
+int launch_attn_fwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
                          const fa_tensor_t* k, const fa_tensor_t* v,
                          const fa_tensor_t* o, float* lse, float scale,
                          cudaStream_t stream) {
   CUtensorMap tq, tk, tv;
   int rc = make_tmap_bshd(&tq, q, sh.B, sh.S, sh.H, sh.D, 128);
   if (rc) return rc;
-  rc = make_tmap_bshd(&tk, k, sh.B, sh.S, sh.H, sh.D, 128);
+  rc = make_tmap_bshd(&tk, k, sh.B, kv_len, sh.H, sh.D, 128);
   if (rc) return rc;
-  rc = make_tmap_bshd(&tv, v, sh.B, sh.S, sh.H, sh.D, 128);
+  rc = make_tmap_bshd(&tv, v, sh.B, kv_len, sh.H, sh.D, 128);
   if (rc) return rc;
   fwd::Params p;
   p.S = sh.S;
   p.H = sh.H;
-  p.nkv = (sh.S + fwd::kKeys - 1) / fwd::kKeys;
+  p.kv_len = kv_len;
+  p.nkv = (kv_len + fwd::kKeys - 1) / fwd::kKeys;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.o = reinterpret_cast<__nv_bfloat16*>(o->data);
   p.os_b = o->stride_b;

@@ -299,7 +299,7 @@ int fa_fwd(int dtype, int B, int S, int H, int D, const fa_tensor_t* q,
     FA_TRY(launch_rope_pair(dtype, sh, q, &qr, k, &kr, rope, 0, 0, st, table));
   }
   cudaEvent_t stop = timer_begin(FA_TIMER_FWD, st);
-  const int rc = bf ? launch_attn_fwd_bf16(sh, &qr, &kr, v, o, lse, scale, st)
+  const int rc = bf ? launch_attn_fwd_bf16(sh, S, &qr, &kr, v, o, lse, scale, st)
                     : launch_attn_fwd_f32(sh, S, &qr, &kr, v, o, lse, scale, st);
   timer_end(stop, st);
   return rc;
@@ -373,7 +373,7 @@ int fa_bwd(int dtype, int B, int S, int H, int D, const fa_tensor_t* q,
     FA_TRY(record_cuda_error(cudaMemsetAsync(dq_acc, 0, acc_bytes, st)));
     cudaEvent_t stop = timer_begin(FA_TIMER_BWD, st);
     const int rc = launch_attn_bwd_bf16(sh, S, &qr, &kr, v, d_o, lse2, delta,
-                                        dq_acc, dk, dv, nullptr, nullptr, scale,
+                                        dq_acc, dk, dv, nullptr, nullptr, 0, scale,
                                         rope, table, st);
     timer_end(stop, st);
     FA_TRY(rc);
@@ -423,18 +423,20 @@ int fa_fwd_partial(int dtype, int B, int S, int kv_len, int H, int D,
                    float* lse_blk, float scale, void* stream) {
   FA_TRY(check_shape(dtype, B, S, H, D));
   if (kv_len <= 0) return FA_ERR_INVALID_ARG;
+  if (!(scale > 0.f) || !std::isfinite(scale)) return FA_ERR_INVALID_ARG;
   const bool bf = dtype == FA_DTYPE_BF16;
   const int es = bf ? 2 : 4;
-  for (const fa_tensor_t* t : {q, k, v, o_blk}) FA_TRY(check_tensor(t, es, bf));
+  for (const fa_tensor_t* t : {q, k, v}) FA_TRY(check_tensor(t, es, bf));
+  FA_TRY(check_tensor(o_blk, es, true));
   if (lse_blk == nullptr) return FA_ERR_INVALID_ARG;
   FA_TRY(check_sm100());
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const AttnShape sh{B, S, H, D};
-  if (bf) {
-    if (kv_len != S) return FA_ERR_UNSUPPORTED;  // equal shards on this path
-    return launch_attn_fwd_bf16(sh, q, k, v, o_blk, lse_blk, scale, st);
-  }
-  return launch_attn_fwd_f32(sh, kv_len, q, k, v, o_blk, lse_blk, scale, st);
+  cudaEvent_t stop = timer_begin(FA_TIMER_FWD, st);
+  const int rc = bf ? launch_attn_fwd_bf16(sh, kv_len, q, k, v, o_blk, lse_blk, scale, st)
+                    : launch_attn_fwd_f32(sh, kv_len, q, k, v, o_blk, lse_blk, scale, st);
+  timer_end(stop, st);
+  return rc;
 }
 
 int fa_lse_merge(int dtype, int B, int S, int H, int D, float* o_acc,
@@ -448,39 +450,65 @@ int fa_lse_merge(int dtype, int B, int S, int H, int D, float* o_acc,
                           lse_blk, first, reinterpret_cast<cudaStream_t>(stream));
 }
 
-int fa_bwd_delta(int dtype, int B, int S, int H, int D, const fa_tensor_t* o,
-                 const fa_tensor_t* d_o, float* delta, void* stream) {
+int fa_bwd_prepare(int dtype, int B, int S, int H, int D, const fa_tensor_t* o,
+                   const fa_tensor_t* d_o, const float* lse, float* lse2_pad,
+                   float* delta_pad, void* stream) {
   FA_TRY(check_shape(dtype, B, S, H, D));
   const int es = dtype == FA_DTYPE_BF16 ? 2 : 4;
   FA_TRY(check_tensor(o, es, false));
   FA_TRY(check_tensor(d_o, es, false));
-  if (delta == nullptr) return FA_ERR_INVALID_ARG;
+  if (lse == nullptr || lse2_pad == nullptr || delta_pad == nullptr) return FA_ERR_INVALID_ARG;
   FA_TRY(check_sm100());
-  return launch_bwd_delta(dtype, AttnShape{B, S, H, D}, o, d_o, nullptr, delta,
-                          nullptr, S, reinterpret_cast<cudaStream_t>(stream));
+  const int s_pad = ((S + 127) / 128) * 128;
+  return launch_bwd_delta(dtype, AttnShape{B, S, H, D}, o, d_o, lse, delta_pad,
+                          lse2_pad, s_pad, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int fa_bwd_partial(int dtype, int B, int S, int kv_len, int H, int D,
                    const fa_tensor_t* q, const fa_tensor_t* k,
                    const fa_tensor_t* v, const fa_tensor_t* d_o,
-                   const float* lse, const float* delta, float* dq_acc,
-                   float* dk_acc, float* dv_acc, float scale, void* stream) {
-  (void)q; (void)k; (void)v; (void)d_o; (void)lse; (void)delta; (void)dq_acc;
-  (void)dk_acc; (void)dv_acc; (void)scale; (void)stream; (void)kv_len;
+                   const float* lse2_pad, const float* delta_pad, float* dq_acc,
+                   float* dk_acc, float* dv_acc, int accumulate, float scale,
+                   void* stream) {
   FA_TRY(check_shape(dtype, B, S, H, D));
-  return FA_ERR_UNSUPPORTED;  // sequence-shard backward: not built yet
+  if (dtype != FA_DTYPE_BF16) return FA_ERR_UNSUPPORTED;
+  if (kv_len <= 0) return FA_ERR_INVALID_ARG;
+  if (!(scale > 0.f) || !std::isfinite(scale)) return FA_ERR_INVALID_ARG;
+  for (const fa_tensor_t* t : {q, k, v, d_o}) FA_TRY(check_tensor(t, 2, true));
+  if (!lse2_pad || !delta_pad || !dq_acc || !dk_acc || !dv_acc) return FA_ERR_INVALID_ARG;
+  for (const void* pp : {(const void*)lse2_pad, (const void*)delta_pad, (const void*)dq_acc,
+                         (const void*)dk_acc, (const void*)dv_acc})
+    if (reinterpret_cast<uintptr_t>(pp) % 16 != 0) return FA_ERR_ALIGNMENT;
+  FA_TRY(check_sm100());
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  cudaEvent_t stop = timer_begin(FA_TIMER_BWD, st);
+  const int rc = launch_attn_bwd_bf16(AttnShape{B, S, H, D}, kv_len, q, k, v, d_o, lse2_pad,
+                                      delta_pad, dq_acc, nullptr, nullptr, dk_acc, dv_acc,
+                                      accumulate, scale, nullptr, nullptr, st);
+  timer_end(stop, st);
+  return rc;
+}
+
+int fa_add_f32(int64_t n, float* dst, const float* src, void* stream) {
+  if (n < 0 || (n > 0 && (dst == nullptr || src == nullptr))) return FA_ERR_INVALID_ARG;
+  if (reinterpret_cast<uintptr_t>(dst) % 16 != 0 || reinterpret_cast<uintptr_t>(src) % 16 != 0)
+    return FA_ERR_ALIGNMENT;
+  if (n == 0) return FA_OK;
+  FA_TRY(check_sm100());
+  return launch_add_f32(n, dst, src, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int fa_cast_f32(int dtype, int B, int S, int H, int D, const float* x,
-                const fa_tensor_t* y, float alpha, const fa_rope_t* rope,
-                void* stream) {
+                int x_layout, const fa_tensor_t* y, float alpha,
+                const fa_rope_t* rope, void* stream) {
   FA_TRY(check_shape(dtype, B, S, H, D));
   FA_TRY(check_rope(rope, D));
-  if (x == nullptr) return FA_ERR_INVALID_ARG;
+  if (x == nullptr || (x_layout != 0 && x_layout != 1)) return FA_ERR_INVALID_ARG;
   FA_TRY(check_tensor(y, dtype == FA_DTYPE_BF16 ? 2 : 4, false));
   FA_TRY(check_sm100());
+  const int s_pad = x_layout == 1 ? ((S + 127) / 128) * 128 : 0;
   return launch_cast_f32(dtype, AttnShape{B, S, H, D}, x, y, alpha, rope, 0,
-                         reinterpret_cast<cudaStream_t>(stream));
+                         reinterpret_cast<cudaStream_t>(stream), nullptr, s_pad);
 }
 
 int fa_timing_enable(int on) {

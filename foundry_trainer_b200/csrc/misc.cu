@@ -266,6 +266,24 @@ __global__ void lse_merge_kernel(float* o_acc, float* lse_acc, TView o_blk,
   if (lane == 0) lse_acc[li] = mx + logf(wa + wb);
 }
 
+__global__ void add_f32_kernel(int64_t n4, float4* dst, const float4* src) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float4 a = dst[i];
+    const float4 b = src[i];
+    a.x += b.x;
+    a.y += b.y;
+    a.z += b.z;
+    a.w += b.w;
+    dst[i] = a;
+  }
+}
+
+__global__ void add_f32_tail_kernel(int64_t n, float* dst, const float* src) {
+  const int64_t i = threadIdx.x;
+  if (i < n) dst[i] += src[i];
+}
+
 TView tview(const fa_tensor_t* t) { return TView{t->data, t->stride_b, t->stride_s, t->stride_h}; }
 TOut tout(const fa_tensor_t* t) { return TOut{t->data, t->stride_b, t->stride_s, t->stride_h}; }
 
@@ -403,6 +421,19 @@ int launch_cast_f32(int dtype, const AttnShape& sh, const float* x,
                 : misc::TView{x, (int64_t)sh.S * sh.H * D, (int64_t)sh.H * D, D};
   return launch_rope_generic(FA_DTYPE_F32, dtype, sh, xv, misc::tout(y), r,
                              alpha, 1, stream);
+}
+
+int launch_add_f32(int64_t n, float* dst, const float* src, cudaStream_t stream) {
+  const int64_t n4 = n / 4;
+  if (n4 > 0) {
+    // 148 SMs x 8 blocks of 256 threads, grid-stride over float4
+    const int64_t blocks = std::min<int64_t>((n4 + 255) / 256, 148 * 8);
+    misc::add_f32_kernel<<<(unsigned)blocks, 256, 0, stream>>>(
+        n4, reinterpret_cast<float4*>(dst), reinterpret_cast<const float4*>(src));
+  }
+  if (n % 4 != 0)
+    misc::add_f32_tail_kernel<<<1, 32, 0, stream>>>(n % 4, dst + 4 * n4, src + 4 * n4);
+  return launch_status();
 }
 
 int launch_lse_merge(int dtype, const AttnShape& sh, float* o_acc,

@@ -98,7 +98,7 @@ extern "C" int fa_bwd_noalloc(int B, int S, int H, int D, const fa_tensor_t* q,
   rc = record_cuda_error(cudaMemsetAsync(dq_acc, 0, rows * D * 4, st));
   if (rc != FA_OK) return rc;
   rc = launch_attn_bwd_bf16(sh, S, q, k, v, d_o, lse2, delta, dq_acc, dk, dv,
-                            nullptr, nullptr, scale, nullptr, nullptr, st);
+                            nullptr, nullptr, 0, scale, nullptr, nullptr, st);
   if (rc != FA_OK) return rc;
   return launch_cast_f32(FA_DTYPE_BF16, sh, dq_acc, dq, scale, nullptr, 0, st,
                          nullptr, s_pad);

@@ -125,23 +125,31 @@ int fa_rope_apply(int dtype, int B, int S, int H, int D, const fa_tensor_t* x,
 
 /*
  * Sequence-parallel (ring) building blocks. They have no counterpart in the
- * reference, which is single-GPU (SURVEY: no collectives anywhere); they let a
- * host driver rotate K/V shards between ranks and fold each block into the
- * local result.
+ * reference, which is single-GPU (it has no collectives); they let a host
+ * driver rotate K/V shards between ranks and fold each block into the local
+ * result. q/k passed here are already rotated (fa_rope_apply with the
+ * shard's positions).
  *
- * fa_fwd_partial: like fa_fwd on one K/V block (kv_len keys, rows indexed
- *   by the block), writing an un-normalised-free partial (o_blk, lse_blk); the
- *   caller merges blocks with fa_lse_merge. q rows are S; keys are kv_len.
- * fa_lse_merge: (o_acc, lse_acc) <- merge((o_acc, lse_acc), (o_blk, lse_blk))
- *   with o_acc fp32 (B,S,H,D) contiguous and o_blk in `dtype`; first != 0
- *   initialises from the block.
- * fa_bwd_partial: one K/V block of the backward: accumulates scale*dS*K into
- *   the fp32 dq_acc (B,S,H,D contiguous) and adds the block's dK, dV into the
- *   fp32 dk_acc, dv_acc (B,kv_len,H,D contiguous). `delta` is the per-row
- *   rowsum(dO*O) (B,H,S) from fa_bwd_delta.
- * fa_bwd_delta: delta[b,h,s] = sum_d dO*O in fp32.
- * fa_cast_f32: y(dtype) = x(fp32 contiguous B,S,H,D) * alpha, with the inverse
- *   rotation applied when rope is non-NULL.
+ * fa_fwd_partial: attention of the S local query rows against one block of
+ *   kv_len keys: o_blk = softmax(q k_blk^T * scale) v_blk, normalised over the
+ *   block, and its log-sum-exp lse_blk (fp32, contiguous (B,H,S)).
+ * fa_lse_merge: (o_acc, lse_acc) <- merge((o_acc, lse_acc), (o_blk, lse_blk));
+ *   o_acc fp32 contiguous (B,S,H,D), lse_acc (B,H,S); first != 0 initialises
+ *   the accumulator from the block.
+ * fa_bwd_prepare: per local row, lse2_pad = lse * log2(e) and
+ *   delta_pad = rowsum(dO * O), both fp32 (B, H, S_pad) with
+ *   S_pad = ceil(S/128)*128 (padding +inf and 0), from the merged forward
+ *   output o, its gradient d_o and the merged lse.
+ * fa_bwd_partial: one K/V block of the bf16 backward against the S local rows:
+ *   adds dS K (unscaled) into dq_acc (fp32 (B, H, S_pad, D), zeroed by the
+ *   caller before the first block) and writes scale*dS^T Q, P^T dO to dk_acc,
+ *   dv_acc (fp32 contiguous (B, kv_len, H, D)): added to their contents when
+ *   accumulate != 0, stored over them otherwise.
+ * fa_add_f32: dst[i] += src[i] for i < n (fp32, both 16-byte aligned); folds
+ *   a block's dK/dV into the accumulator that arrived from the previous rank.
+ * fa_cast_f32: y = alpha * x converted to `dtype`, un-rotated when rope is
+ *   non-NULL; x is fp32 contiguous (B,S,H,D) (x_layout 0) or (B,H,S_pad,D)
+ *   (x_layout 1, the dq_acc layout).
  */
 int fa_fwd_partial(int dtype, int B, int S, int kv_len, int H, int D,
                    const fa_tensor_t* q, const fa_tensor_t* k,
@@ -150,16 +158,19 @@ int fa_fwd_partial(int dtype, int B, int S, int kv_len, int H, int D,
 int fa_lse_merge(int dtype, int B, int S, int H, int D, float* o_acc,
                  float* lse_acc, const fa_tensor_t* o_blk,
                  const float* lse_blk, int first, void* stream);
-int fa_bwd_delta(int dtype, int B, int S, int H, int D, const fa_tensor_t* o,
-                 const fa_tensor_t* d_o, float* delta, void* stream);
+int fa_bwd_prepare(int dtype, int B, int S, int H, int D, const fa_tensor_t* o,
+                   const fa_tensor_t* d_o, const float* lse, float* lse2_pad,
+                   float* delta_pad, void* stream);
 int fa_bwd_partial(int dtype, int B, int S, int kv_len, int H, int D,
                    const fa_tensor_t* q, const fa_tensor_t* k,
                    const fa_tensor_t* v, const fa_tensor_t* d_o,
-                   const float* lse, const float* delta, float* dq_acc,
-                   float* dk_acc, float* dv_acc, float scale, void* stream);
+                   const float* lse2_pad, const float* delta_pad, float* dq_acc,
+                   float* dk_acc, float* dv_acc, int accumulate, float scale,
+                   void* stream);
+int fa_add_f32(int64_t n, float* dst, const float* src, void* stream);
 int fa_cast_f32(int dtype, int B, int S, int H, int D, const float* x,
-                const fa_tensor_t* y, float alpha, const fa_rope_t* rope,
-                void* stream);
+                int x_layout, const fa_tensor_t* y, float alpha,
+                const fa_rope_t* rope, void* stream);
 
 /*
  * Backward without a caller workspace. This entry point has no counterpart in
