@@ -19,9 +19,11 @@
 //   warps 0-3     softmax backward for queries 0-63 of the tile (one key row
 //                 per thread); dV epilogue
 //   warps 10-13   the same for queries 64-127; dK epilogue
-//   warps 4-7     dQ drain: dQ^T from TMEM, staged as row-major 32-query
-//                 chunks in shared memory, added into dq_acc (B, H, S_pad, D)
-//                 with 16 KB TMA bulk reduce-adds (fp32)
+//   warps 4-7     dQ drain: dQ^T from TMEM, staged row-major (query, d) in
+//                 the step's own Q_i|dO_i slot (64 KB, free once the dQ^T MMA
+//                 has completed), added into dq_acc (B, H, S_pad, D) with TMA
+//                 bulk reduce-adds (fp32); the slot goes back to the producer
+//                 when the reduces have read it
 // TMEM (512 columns):
 //   A [0,128)    S^T_i; after the softmax, per query half h (columns
 //                64h..64h+63): P^T (bf16 pairs, 32 columns) then dS^T (32
@@ -30,9 +32,9 @@
 //                column, column = query)
 //   dV [256,384) dK [384,512)   accumulators over all Q tiles
 // Every MMA that overwrites columns another MMA reads waits for that MMA's
-// commit first; dQ_i is drained while S^T_{i+1} runs. The drain stages through
-// the shared dS^T tile (free once the dQ^T MMA has read it: DQFULL) and hands
-// it back to the softmax warps (DSFREE) once the bulk reduces have read it.
+// commit first; dQ_i is drained while S^T_{i+1} runs, and TMEM B is handed
+// back (DQFREE) as soon as it has been read into registers. The dS^T tile is
+// free for the next step's softmax once the dQ^T MMA has read it (DSFREE).
 #include "attn_common.h"
 #include "rope.cuh"
 #include "sm100_ptx.cuh"
@@ -47,9 +49,11 @@ constexpr int kThreads = 448;
 
 constexpr int kOffK = 0;
 constexpr int kOffV = kOffK + kTileBytes;
-constexpr int kOffQ = kOffV + kTileBytes;     // 2 stages
-constexpr int kOffDO = kOffQ + 2 * kTileBytes;  // 2 stages
-constexpr int kOffDS = kOffDO + 2 * kTileBytes;
+// two stages of [Q_i | dO_i] (64 KB each, contiguous: the dQ_i staging area
+// once the step's MMAs are done)
+constexpr int kOffStage = kOffV + kTileBytes;
+constexpr int kStageBytes = 2 * kTileBytes;
+constexpr int kOffDS = kOffStage + 2 * kStageBytes;
 constexpr int kOffLse = kOffDS + kTileBytes;    // 2 x 512 B
 constexpr int kOffDelta = kOffLse + 1024;       // 2 x 512 B
 constexpr int kOffBar = kOffDelta + 1024;
@@ -243,8 +247,8 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
         const int qrow = q_tile_of(i, kv_tile, nq) * kRows;
         uint64_t* bar = &bars[B_QFULL + st];
         mbar_arrive_expect_tx(bar, 2 * kTileBytes + 1024);
-        uint8_t* qd = smem + kOffQ + st * kTileBytes;
-        uint8_t* dd = smem + kOffDO + st * kTileBytes;
+        uint8_t* qd = smem + kOffStage + st * kStageBytes;
+        uint8_t* dd = qd + kTileBytes;
         tma_load_4d(qd, &tm_q, bar, 0, qrow, h, b);
         tma_load_4d(qd + kBlkBytes, &tm_q, bar, 64, qrow, h, b);
         tma_load_4d(dd, &tm_do, bar, 0, qrow, h, b);
@@ -271,8 +275,8 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
         const int st = i & 1, n = i >> 1;
         if (*abort_flag) { ok = false; break; }
         if (!(ok = mbar_wait(&bars[B_QFULL + st], n & 1))) break;
-        const uint32_t q_base = smem_u32(smem + kOffQ + st * kTileBytes);
-        const uint32_t do_base = smem_u32(smem + kOffDO + st * kTileBytes);
+        const uint32_t q_base = smem_u32(smem + kOffStage + st * kStageBytes);
+        const uint32_t do_base = q_base + kTileBytes;
         // S^T_i = K Q_i^T -> A   (A was read by dV/dK of step i-1)
         if (i > 0 && !(ok = mbar_wait(&bars[B_DVK], (i - 1) & 1))) break;
         tc_fence_after();
@@ -304,13 +308,13 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                   mnmajor_desc(q_base, kk, kBlkBytes), kIdKM,
                   (i > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&bars[B_DVK]);
-        umma_commit(&bars[B_QEMPTY + st]);
         // dQ^T_i = K^T dS^T_i -> B   (both operands MN-major in shared memory)
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
           umma_ss(tmem + kColB, mnmajor_desc(k_base, kk, kBlkBytes),
                   mnmajor_desc(ds_base, kk, kBlkBytes), kIdMM, kk > 0);
         umma_commit(&bars[B_DQFULL]);
+        umma_commit(&bars[B_DSFREE]);
       }
       if (!ok) *abort_flag = 1;
       umma_commit(&bars[B_FINAL]);
@@ -374,8 +378,8 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
         tmem_st8(t_a + 32 + cb * 8, dk);  // dS^T: columns 64h + [32, 64)
       }
       tmem_wait_st();
-      // dS^T also goes to shared memory (B operand of dQ^T), once the drain
-      // of dQ_{i-1} has released the tile: read back this half's 32 packed
+      // dS^T also goes to shared memory (B operand of dQ^T), once the dQ^T
+      // MMA of step i-1 has read the tile: read back this half's 32 packed
       // columns and store them as 16-byte chunks 0-7 of swizzle block h.
       if (i > 0) {
         ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_DSFREE], (i - 1) & 1));
@@ -427,14 +431,11 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
     const uint32_t lane_off = (uint32_t)(sub * 32) << 16;
     const uint32_t t_b = tmem + lane_off + kColB;
     const bool leader = (warp == 4 && lane == 0);
-    // two 16 KB staging chunks (32 queries x 128 fp32, row-major) in the
-    // shared dS^T tile; a thread writes column d, a warp 128 contiguous bytes
-    float* stage_a = reinterpret_cast<float*>(smem + kOffDS);
-    float* stage_b = stage_a + 32 * 128;
     float* dq_bh = p.dq_acc + ((int64_t)b * p.H + h) * p.s_pad * 128;
+    // a thread writes column d of 64 query rows; a warp 128 contiguous bytes
     auto stage = [&](float* buf, const uint32_t* v) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) buf[j * 128 + d] = __uint_as_float(v[j]);
+      for (int j = 0; j < 64; ++j) buf[j * 128 + d] = __uint_as_float(v[j]);
     };
     for (int i = 0; i < nq; ++i) {
       // leave together: the staging uses a named barrier over warps 4-7
@@ -442,38 +443,30 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
       if (!stop) stop = !mbar_wait(&bars[B_DQFULL], i & 1);
       if (named_bar_any(2, 128, stop)) break;
       tc_fence_after();
+      const int st = i & 1;
+      // the step's Q_i | dO_i slot: every MMA reading it completed before DQFULL
+      float* buf = reinterpret_cast<float*>(smem + kOffStage + st * kStageBytes);
       float* dst = dq_bh + (int64_t)q_tile_of(i, kv_tile, nq) * kRows * 128;
-      uint32_t r0[32], r1[32];
-      tmem_ld32(t_b + 0, r0);
-      tmem_ld32(t_b + 32, r1);
+      uint32_t r[64];
+      tmem_ld32(t_b + 0, r);
+      tmem_ld32(t_b + 32, r + 32);
       tmem_wait_ld();
-      stage(stage_a, r0);
-      stage(stage_b, r1);
-      fence_proxy_async_smem();
-      named_bar_sync(2, 128);
-      if (leader) {
-        bulk_reduce_add_f32(dst, stage_a, 16384);
-        bulk_reduce_add_f32(dst + 32 * 128, stage_b, 16384);
-        bulk_commit_group();
-      }
-      // queries 64-127 into registers; then TMEM B can take dP^T_{i+1}
-      tmem_ld32(t_b + 64, r0);
-      tmem_ld32(t_b + 96, r1);
+      stage(buf, r);
+      tmem_ld32(t_b + 64, r);
+      tmem_ld32(t_b + 96, r + 32);
       tmem_wait_ld();
+      // TMEM B can take dP^T_{i+1}
       tc_fence_before();
       mbar_arrive(&bars[B_DQFREE]);
-      if (leader) bulk_wait_group_read0();
-      named_bar_sync(2, 128);
-      stage(stage_a, r0);
-      stage(stage_b, r1);
+      stage(buf + 64 * 128, r);
       fence_proxy_async_smem();
       named_bar_sync(2, 128);
       if (leader) {
-        bulk_reduce_add_f32(dst + 64 * 128, stage_a, 16384);
-        bulk_reduce_add_f32(dst + 96 * 128, stage_b, 16384);
+        bulk_reduce_add_f32(dst, buf, 32768);
+        bulk_reduce_add_f32(dst + 64 * 128, buf + 64 * 128, 32768);
         bulk_commit_group();
         bulk_wait_group_read0();
-        mbar_arrive(&bars[B_DSFREE]);
+        mbar_arrive(&bars[B_QEMPTY + st]);  // the producer may reload the slot
       }
     }
     if (leader) bulk_wait_group0();  // reductions complete before exit

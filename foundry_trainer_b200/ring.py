@@ -152,7 +152,7 @@ def ring_fwd(q, k, v, pos, scale, comm: RingComm, kern):
             works = comm.exchange(cur, nxt)
         kern.fwd_partial(q_r, cur[0], cur[1], scale, o_blk, lse_blk)
         kern.lse_merge(o_acc, lse, o_blk, lse_blk, t == 0)
-        if works:
+        if t < comm.world - 1:
             comm.wait(works)
             cur = nxt
     o = kern.cast(o_acc, 0, 1.0, None, torch.empty((B, S, H, D), device=dev, dtype=q.dtype))
@@ -194,7 +194,7 @@ def ring_bwd(q_r, k_r, v, o, d_o, lse, pos, scale, comm: RingComm, kern):
             # pass the shard's accumulator on; after the last step it reaches its owner
             acc_works = comm.exchange([acc[a_cur]], [acc[1 - a_cur]])
             a_cur = 1 - a_cur
-        if kv_works:
+        if t < W - 1:
             comm.wait(kv_works)
             cur_kv = nxt_kv
     comm.wait(acc_works)

@@ -47,17 +47,26 @@ def _check(shards, ref, label):
         assert err <= TOL, (label, name, err)
 
 
-def _rank(world, rank, comm, q, k, v, d_o, pos):
-    from foundry_trainer_b200 import ring
+def _rank(world, rank, comm, q, k, v, d_o, pos, autograd=True):
+    from foundry_trainer_b200 import ops, ring
     n = q.shape[1] // world
     sl = slice(rank * n, (rank + 1) * n)
-    to = lambda t: t[:, sl].to(torch.bfloat16).cuda().requires_grad_(True)
-    qs, ks, vs = to(q), to(k), to(v)
-    o = ring.ring_attention(qs, ks, vs, pos=pos[sl].contiguous().cuda(), comm=comm)
-    o.backward(d_o[:, sl].to(torch.bfloat16).cuda())
-    torch.cuda.synchronize()
+    to = lambda t: t[:, sl].to(torch.bfloat16).cuda()
+    qs, ks, vs, dos, ps = to(q), to(k), to(v), to(d_o), pos[sl].contiguous().cuda()
     f = lambda t: t.detach().float().cpu().numpy()
-    return f(o), f(qs.grad), f(ks.grad), f(vs.grad)
+    if autograd:
+        qs, ks, vs = (t.requires_grad_(True) for t in (qs, ks, vs))
+        o = ring.ring_attention(qs, ks, vs, pos=ps, comm=comm)
+        o.backward(dos)
+        torch.cuda.synchronize()
+        return f(o), f(qs.grad), f(ks.grad), f(vs.grad)
+    # the autograd engine runs every CUDA backward of a device on one worker
+    # thread, so threads standing in for ranks call the ring directly
+    kern, scale = ring.RingKernels(), ops.default_scale(128)
+    o, lse, q_r, k_r = ring.ring_fwd(qs, ks, vs, ps, scale, comm, kern)
+    dq, dk, dv = ring.ring_bwd(q_r, k_r, vs, o, dos, lse, ps, scale, comm, kern)
+    torch.cuda.synchronize()
+    return f(o), f(dq), f(dk), f(dv)
 
 
 def test_ring_single_rank_matches_oracle():
@@ -77,7 +86,7 @@ def test_ring_thread_emulated_ranks_match_oracle(world, S):
 
     def body(r):
         try:
-            outs[r] = _rank(world, r, ring_.comm(r), q, k, v, d_o, pos)
+            outs[r] = _rank(world, r, ring_.comm(r), q, k, v, d_o, pos, autograd=False)
         except BaseException as e:  # surfaced below
             errors.append(e)
             ring_.barrier.abort()
