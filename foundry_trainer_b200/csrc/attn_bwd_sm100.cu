@@ -120,16 +120,16 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src,
       : "memory");
 }
 
-// Writes columns [col0, col0+64) of one dK/dV row held in registers.
-__device__ __forceinline__ void store_half_row(const Params& p, bool is_dk,
-                                               int b, int key, int h, int col0,
-                                               const float* v) {
+// Writes columns [col0, col0+32) of one dK/dV row held in registers.
+__device__ __forceinline__ void store_chunk32(const Params& p, bool is_dk, int b,
+                                              int key, int h, int col0,
+                                              const float* v) {
   if (p.acc) {
     float* dst = (is_dk ? p.dk_acc : p.dv_acc) +
                  (((int64_t)b * p.kv_len + key) * p.H + h) * 128 + col0;
     float4* d4 = reinterpret_cast<float4*>(dst);
 #pragma unroll
-    for (int c = 0; c < 16; ++c) {
+    for (int c = 0; c < 8; ++c) {
       float4 o = make_float4(v[4 * c + 0], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
       if (p.acc == 1) {
         const float4 a = d4[c];
@@ -149,7 +149,7 @@ __device__ __forceinline__ void store_half_row(const Params& p, bool is_dk,
         col0;
     uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
+    for (int c = 0; c < 4; ++c) {
       uint4 o;
       o.x = pack_bf16(v[8 * c + 0], v[8 * c + 1]);
       o.y = pack_bf16(v[8 * c + 2], v[8 * c + 3]);
@@ -160,19 +160,27 @@ __device__ __forceinline__ void store_half_row(const Params& p, bool is_dk,
   }
 }
 
-// Inverse rotation of columns [col0, col0+64) (two 32-wide axis segments).
-__device__ __forceinline__ void unrotate_half_row(const RopeArgs& r, int token,
-                                                  int col0, float* v) {
+// (cos, sin) of the 16 frequencies of 32-wide axis `a` for `token`, from the
+// table: 128 contiguous bytes, 8 independent 16-byte loads.
+__device__ __forceinline__ void load_axis_cs(const RopeArgs& r, int token, int a,
+                                             float4* cs) {
+  const float4* t4 = reinterpret_cast<const float4*>(
+      r.table + (int64_t)(token + r.pos_offset) * (r.n_axes * (r.axis_dim >> 1)) + a * 16);
 #pragma unroll
-  for (int a = 0; a < 2; ++a) {
+  for (int u = 0; u < 8; ++u) cs[u] = t4[u];
+}
+
+// Inverse rotation of one 32-wide axis segment held in v[0..32).
+__device__ __forceinline__ void unrotate_axis(const float4* cs, float* v) {
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const float2 cs = rope_cs(r, token, (col0 / 32 + a) * 16 + j);
-      const float x1 = v[a * 32 + j];
-      const float x2 = v[a * 32 + j + 16];
-      v[a * 32 + j] = __fadd_rn(__fmul_rn(x1, cs.x), __fmul_rn(x2, cs.y));
-      v[a * 32 + j + 16] = __fadd_rn(__fmul_rn(x2, cs.x), __fmul_rn(-x1, cs.y));
-    }
+  for (int j = 0; j < 16; ++j) {
+    const float4 q = cs[j >> 1];
+    const float c = (j & 1) ? q.z : q.x;
+    const float sn = (j & 1) ? q.w : q.y;
+    const float x1 = v[j];
+    const float x2 = v[j + 16];
+    v[j] = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x2, sn));
+    v[j + 16] = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(-x1, sn));
   }
 }
 
@@ -399,27 +407,36 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
       mbar_arrive(&bars[B_PS]);
     }
     // epilogue: warps 0-3 store dV, warps 10-13 store dK (scaled, and
-    // un-rotated when the op owns the RoPE), 64 columns at a time
+    // un-rotated when the op owns the RoPE), one 32-column axis at a time;
+    // the (cos, sin) of the next axis are loaded while this one is stored,
+    // the first before the wait for the last MMA
+    const bool is_dk = half == 1;
+    const int key = kv_tile * kRows + key_in_tile;
+    const bool unrot = is_dk && p.rope.pos != nullptr && p.rope.table != nullptr &&
+                       key < p.kv_len;
+    float4 cs[8], cs_next[8];
+    if (unrot) load_axis_cs(p.rope, key, 0, cs);
     if (ok && __all_sync(0xffffffffu, mbar_wait(&bars[B_FINAL], 0)) &&
         !__any_sync(0xffffffffu, *abort_flag != 0)) {
       tc_fence_after();
-      const bool is_dk = half == 1;
       const uint32_t t_acc = tmem + lane_off + (is_dk ? kColDK : kColDV);
-      const int key = kv_tile * kRows + key_in_tile;
 #pragma unroll
-      for (int hc = 0; hc < 2; ++hc) {
-        uint32_t r[64];
-        tmem_ld32(t_acc + hc * 64, r);
-        tmem_ld32(t_acc + hc * 64 + 32, r + 32);
+      for (int a = 0; a < 4; ++a) {
+        uint32_t r[32];
+        tmem_ld32(t_acc + a * 32, r);
+        if (unrot && a < 3) load_axis_cs(p.rope, key, a + 1, cs_next);
         tmem_wait_ld();
         float* v = reinterpret_cast<float*>(r);
         if (is_dk) {
 #pragma unroll
-          for (int c = 0; c < 64; ++c) v[c] *= p.scale;
-          if (p.rope.pos != nullptr && key < p.kv_len)
-            unrotate_half_row(p.rope, key, hc * 64, v);
+          for (int c = 0; c < 32; ++c) v[c] *= p.scale;
+          if (unrot) unrotate_axis(cs, v);
         }
-        if (key < p.kv_len) store_half_row(p, is_dk, b, key, h, hc * 64, v);
+        if (key < p.kv_len) store_chunk32(p, is_dk, b, key, h, a * 32, v);
+        if (unrot && a < 3) {
+#pragma unroll
+          for (int u = 0; u < 8; ++u) cs[u] = cs_next[u];
+        }
       }
     } else {
       *abort_flag = 1;
@@ -493,6 +510,8 @@ int launch_attn_bwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
                          cudaStream_t stream) {
   if (rope != nullptr && (rope->axis_dim != 32 || rope->n_axes != 4))
     return FA_ERR_UNSUPPORTED;  // the dK epilogue un-rotates 32-wide axes
+  if (rope != nullptr && rope_table == nullptr)
+    return FA_ERR_INVALID_ARG;  // ... with the (cos, sin) table
   CUtensorMap tq, tk, tv, tdo;
   int rc = make_tmap_bshd(&tq, q, sh.B, sh.S, sh.H, sh.D, 128);
   if (!rc) rc = make_tmap_bshd(&tk, k, sh.B, kv_len, sh.H, sh.D, 128);

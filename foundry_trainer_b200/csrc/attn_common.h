@@ -84,10 +84,13 @@ int launch_rope_table(int dtype, int S, const fa_rope_t* rope, int pos_offset,
 int launch_rope(int dtype, const AttnShape& sh, const fa_tensor_t* x,
                 const fa_tensor_t* y, const fa_rope_t* rope, int inverse,
                 int pos_offset, cudaStream_t stream, const float2* table = nullptr);
+// table: (cos, sin) to read, or nullptr to evaluate them; table_out: where
+// the token-major path also writes the evaluated values (nullptr: nowhere)
 int launch_rope_pair(int dtype, const AttnShape& sh, const fa_tensor_t* x0,
                      const fa_tensor_t* y0, const fa_tensor_t* x1,
                      const fa_tensor_t* y1, const fa_rope_t* rope, int inverse,
-                     int pos_offset, cudaStream_t stream, const float2* table);
+                     int pos_offset, cudaStream_t stream, const float2* table,
+                     float2* table_out = nullptr);
 // x: fp32 (B, S, H, D) contiguous, or (B, H, s_pad, D) when s_pad > 0
 int launch_cast_f32(int dtype, const AttnShape& sh, const float* x,
                     const fa_tensor_t* y, float alpha, const fa_rope_t* rope,

@@ -265,7 +265,7 @@ size_t fa_fwd_workspace_bytes(int dtype, int B, int S, int H, int D,
                               const fa_rope_t* rope) {
   if (rope == nullptr) return 0;
   const size_t es = dtype == FA_DTYPE_BF16 ? 2 : 4;
-  return rope_table_bytes(S, rope) + 2 * align256((size_t)B * S * H * D * es);
+  return 2 * align256((size_t)B * S * H * D * es);
 }
 
 int fa_fwd(int dtype, int B, int S, int H, int D, const fa_tensor_t* q,
@@ -290,13 +290,10 @@ int fa_fwd(int dtype, int B, int S, int H, int D, const fa_tensor_t* q,
     const size_t need = fa_fwd_workspace_bytes(dtype, B, S, H, D, rope);
     if (workspace == nullptr || workspace_bytes < need) return FA_ERR_WORKSPACE;
     uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
-    float2* table = reinterpret_cast<float2*>(ws);
-    ws += rope_table_bytes(S, rope);
     const size_t tb = align256((size_t)B * S * H * D * es);
     qr = contiguous_view(ws, S, H, D);
     kr = contiguous_view(ws + tb, S, H, D);
-    FA_TRY(launch_rope_table(dtype, S, rope, 0, table, st));
-    FA_TRY(launch_rope_pair(dtype, sh, q, &qr, k, &kr, rope, 0, 0, st, table));
+    FA_TRY(launch_rope_pair(dtype, sh, q, &qr, k, &kr, rope, 0, 0, st, nullptr));
   }
   cudaEvent_t stop = timer_begin(FA_TIMER_FWD, st);
   const int rc = bf ? launch_attn_fwd_bf16(sh, S, &qr, &kr, v, o, lse, scale, st)
@@ -352,7 +349,6 @@ int fa_bwd(int dtype, int B, int S, int H, int D, const fa_tensor_t* q,
   if (rope) {
     table = reinterpret_cast<float2*>(ws);
     ws += rope_table_bytes(S, rope);
-    FA_TRY(launch_rope_table(dtype, S, rope, 0, table, st));
   }
   if (bf) {
     if (rope) {
@@ -360,7 +356,9 @@ int fa_bwd(int dtype, int B, int S, int H, int D, const fa_tensor_t* q,
       ws += align256(n * 2);
       kr = contiguous_view(ws, S, H, D);
       ws += align256(n * 2);
-      FA_TRY(launch_rope_pair(dtype, sh, q, &qr, k, &kr, rope, 0, 0, st, table));
+      // the rotation pass also writes the (cos, sin) table the dK epilogue
+      // and the dQ finish read
+      FA_TRY(launch_rope_pair(dtype, sh, q, &qr, k, &kr, rope, 0, 0, st, nullptr, table));
     }
     const int s_pad = ((S + 127) / 128) * 128;
     float* lse2 = reinterpret_cast<float*>(ws);
@@ -390,7 +388,7 @@ int fa_bwd(int dtype, int B, int S, int H, int D, const fa_tensor_t* q,
     ws += align256(n * 4);
     dkr = contiguous_view(ws, S, H, D);
     ws += align256(n * 4);
-    FA_TRY(launch_rope_pair(dtype, sh, q, &qr, k, &kr, rope, 0, 0, st, table));
+    FA_TRY(launch_rope_pair(dtype, sh, q, &qr, k, &kr, rope, 0, 0, st, nullptr, table));
   }
   float* delta = reinterpret_cast<float*>(ws);
   FA_TRY(launch_bwd_delta(dtype, sh, o, d_o, lse, delta, nullptr, S, st));

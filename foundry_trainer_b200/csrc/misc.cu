@@ -108,14 +108,14 @@ __global__ void rope_warp_kernel(TView x0, TOut y0, TView x1, TOut y1, RopeArgs 
 
 // (cos, sin) per (token, frequency), rounded to the compute dtype: evaluated
 // once per call and reused by every head, batch and kernel of that call.
-__global__ void rope_table_kernel(RopeArgs r, int S, float2* table) {
+// __grid_constant__: inv_freq is indexed in parameter space, not copied to
+// local memory per thread.
+__global__ void rope_table_kernel(const __grid_constant__ RopeArgs r, int S, float2* table) {
   const int nf = r.n_axes * (r.axis_dim >> 1);
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)S * nf) return;
   const int t = (int)(i / nf), f = (int)(i % nf);
-  RopeArgs direct = r;
-  direct.table = nullptr;
-  table[(int64_t)(t + r.pos_offset) * nf + f] = rope_cs(direct, t, f);
+  table[(int64_t)(t + r.pos_offset) * nf + f] = rope_cs_direct(r, t, f);
 }
 
 // ------------------------------------------------ token-major fast paths
@@ -148,70 +148,126 @@ struct Vec4<__nv_bfloat16> {
 };
 
 // y = alpha * rot(x) (or the inverse rotation); blockIdx.x = token (b, s),
-// blockIdx.y selects the (x, y) pair.
+// blockIdx.y selects the (x, y) pair. Four warps; each first issues the loads
+// of up to eight head rows, then the token's 64 (cos, sin) pairs are read
+// from the table (or evaluated, without one) into shared memory while those
+// loads are in flight, and the rows are rotated and stored.
+constexpr int kRopeWarps = 4;
+constexpr int kRopeRowsPerWarp = 8;
 template <typename Tin, typename Tout>
-__global__ void rope_token_kernel(TView x0, TOut y0, TView x1, TOut y1,
-                                  RopeArgs r, int S, int H, float alpha,
-                                  int inverse) {
+__global__ void __launch_bounds__(32 * kRopeWarps)
+rope_token_kernel(TView x0, TOut y0, TView x1, TOut y1,
+                  const __grid_constant__ RopeArgs r, int S, int H, float alpha,
+                  int inverse) {
+  __shared__ float2 cs_s[64];
   const TView& x = blockIdx.y == 0 ? x0 : x1;
   const TOut& y = blockIdx.y == 0 ? y0 : y1;
   const int s = (int)(blockIdx.x % S), b = (int)(blockIdx.x / S);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float c[4], sn[4];
   const bool rotate = r.pos != nullptr;
   const bool first = (lane & 7) < 4;  // element in the first half of its axis
-  if (rotate) {
-    const float4* tab = reinterpret_cast<const float4*>(
-        r.table + (int64_t)(s + r.pos_offset) * 64 + (lane >> 3) * 16 + (lane & 3) * 4);
-    const float4 t0 = tab[0], t1 = tab[1];
-    c[0] = t0.x; sn[0] = t0.y; c[1] = t0.z; sn[1] = t0.w;
-    c[2] = t1.x; sn[2] = t1.y; c[3] = t1.z; sn[3] = t1.w;
-  }
   // forward: first half y = x c - x' s, second half y = x c + x' s;
   // inverse: the transposed rotation (signs swapped)
   const float sgn = (first != (inverse != 0)) ? -1.f : 1.f;
-  for (int h = warp; h < H; h += blockDim.x >> 5) {
-    const Tin* px = reinterpret_cast<const Tin*>(x.p) + b * x.sb + s * x.ss + h * x.sh + 4 * lane;
-    Tout* py = reinterpret_cast<Tout*>(y.p) + b * y.sb + s * y.ss + h * y.sh + 4 * lane;
-    float v[4];
-    Vec4<Tin>::load(px, v);
+  const int f0 = (lane >> 3) * 16 + (lane & 3) * 4;  // lane's frequencies f0..f0+3
+  float v[kRopeRowsPerWarp][4];
+  auto load_rows = [&](int h0) {
 #pragma unroll
-    for (int u = 0; u < 4; ++u) v[u] *= alpha;
-    if (rotate) {
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const float other = __shfl_xor_sync(0xffffffffu, v[u], 4);
-        v[u] = __fadd_rn(__fmul_rn(v[u], c[u]), __fmul_rn(sgn * other, sn[u]));
-      }
+    for (int k = 0; k < kRopeRowsPerWarp; ++k) {
+      const int h = h0 + k * kRopeWarps;
+      if (h < H)
+        Vec4<Tin>::load(reinterpret_cast<const Tin*>(x.p) + b * x.sb + s * x.ss + h * x.sh + 4 * lane,
+                        v[k]);
     }
-    Vec4<Tout>::store(py, v);
+  };
+  load_rows(warp);
+  float c[4], sn[4];
+  if (rotate && threadIdx.x < 64) {
+    const int64_t ti = (int64_t)(s + r.pos_offset) * 64 + threadIdx.x;
+    const float2 t = r.table != nullptr ? r.table[ti] : rope_cs_direct(r, s, threadIdx.x);
+    cs_s[threadIdx.x] = t;
+    if (r.table_out != nullptr && b == 0 && blockIdx.y == 0) r.table_out[ti] = t;
+  }
+  __syncthreads();
+  if (rotate) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      c[u] = cs_s[f0 + u].x;
+      sn[u] = cs_s[f0 + u].y;
+    }
+  }
+  for (int h0 = warp; h0 < H; h0 += kRopeRowsPerWarp * kRopeWarps) {
+    if (h0 != warp) load_rows(h0);
+#pragma unroll
+    for (int k = 0; k < kRopeRowsPerWarp; ++k) {
+      const int h = h0 + k * kRopeWarps;
+      if (h >= H) break;  // uniform across the warp
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[k][u] *= alpha;
+      if (rotate) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float other = __shfl_xor_sync(0xffffffffu, v[k][u], 4);
+          v[k][u] = __fadd_rn(__fmul_rn(v[k][u], c[u]), __fmul_rn(sgn * other, sn[u]));
+        }
+      }
+      Vec4<Tout>::store(reinterpret_cast<Tout*>(y.p) + b * y.sb + s * y.ss + h * y.sh + 4 * lane,
+                        v[k]);
+    }
   }
 }
 
 // delta[b, h, s] = sum_d dO * O over s < s_pad (0 past S); lse2 likewise
-// (+inf past S). One block per token (b, s), one warp per head.
+// (+inf past S). One block per 8 tokens of one b: each warp reduces rows
+// (token, head) four at a time (a lane holds 4 elements of each), the sums
+// meet in shared memory and every head's 8 results leave as one 32-byte
+// store.
+constexpr int kDeltaTokens = 8;
+constexpr int kDeltaMaxHeads = 64;
 template <typename T>
-__global__ void delta_token_kernel(TView o, TView d_o, const float* lse,
-                                   float* delta, float* lse2, int S, int H,
-                                   int s_pad) {
-  const int s = (int)(blockIdx.x % s_pad), b = (int)(blockIdx.x / s_pad);
+__global__ void __launch_bounds__(256)
+delta_token_kernel(TView o, TView d_o, const float* lse, float* delta,
+                   float* lse2, int S, int H, int s_pad) {
+  __shared__ float sums[kDeltaMaxHeads][kDeltaTokens];
+  const int tiles = s_pad / kDeltaTokens;
+  const int s0 = (int)(blockIdx.x % tiles) * kDeltaTokens, b = (int)(blockIdx.x / tiles);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int h = warp; h < H; h += blockDim.x >> 5) {
-    float acc = 0.f;
-    if (s < S) {
-      float a[4], g[4];
-      Vec4<T>::load(reinterpret_cast<const T*>(o.p) + b * o.sb + s * o.ss + h * o.sh + 4 * lane, a);
-      Vec4<T>::load(reinterpret_cast<const T*>(d_o.p) + b * d_o.sb + s * d_o.ss + h * d_o.sh + 4 * lane, g);
-      acc = a[0] * g[0] + a[1] * g[1] + a[2] * g[2] + a[3] * g[3];
+  const int rows = kDeltaTokens * H;
+  for (int r0 = warp * 4; r0 < rows; r0 += (blockDim.x >> 5) * 4) {
+    float acc[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int r = r0 + u;
+      const int t = r / H, h = r % H;
+      const int s = s0 + t;
+      acc[u] = 0.f;
+      if (r < rows && s < S) {
+        float a[4], g[4];
+        Vec4<T>::load(reinterpret_cast<const T*>(o.p) + b * o.sb + s * o.ss + h * o.sh + 4 * lane, a);
+        Vec4<T>::load(reinterpret_cast<const T*>(d_o.p) + b * d_o.sb + s * d_o.ss + h * d_o.sh + 4 * lane, g);
+        acc[u] = a[0] * g[0] + a[1] * g[1] + a[2] * g[2] + a[3] * g[3];
+      }
     }
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-    if (lane == 0) {
-      const int64_t bh = (int64_t)b * H + h;
-      delta[bh * s_pad + s] = acc;
-      if (lse2 != nullptr)
-        lse2[bh * s_pad + s] = (s < S) ? lse[bh * S + s] * 1.4426950408889634f : INFINITY;
+    for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+      for (int u = 0; u < 4; ++u) acc[u] += __shfl_xor_sync(0xffffffffu, acc[u], off);
+    if (lane < 4) {
+      const int r = r0 + lane;
+      float v = acc[0];
+#pragma unroll
+      for (int u = 1; u < 4; ++u) v = lane == u ? acc[u] : v;
+      if (r < rows) sums[r % H][r / H] = v;
     }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < H * kDeltaTokens; i += blockDim.x) {
+    const int h = i / kDeltaTokens, t = i % kDeltaTokens;
+    const int64_t bh = (int64_t)b * H + h;
+    const int s = s0 + t;
+    delta[bh * s_pad + s] = sums[h][t];
+    if (lse2 != nullptr)
+      lse2[bh * s_pad + s] = (s < S) ? lse[bh * S + s] * 1.4426950408889634f : INFINITY;
   }
 }
 
@@ -302,8 +358,9 @@ int launch_bwd_delta(int dtype, const AttnShape& sh, const fa_tensor_t* o,
                      const fa_tensor_t* d_o, const float* lse, float* delta,
                      float* lse2, int s_pad, cudaStream_t stream) {
   const misc::TView ov = misc::tview(o), dv = misc::tview(d_o);
-  if (sh.D == 128 && aligned16(ov, dtype) && aligned16(dv, dtype)) {
-    const dim3 grid((unsigned)((int64_t)sh.B * s_pad));
+  if (sh.D == 128 && sh.H <= misc::kDeltaMaxHeads && s_pad % misc::kDeltaTokens == 0 &&
+      aligned16(ov, dtype) && aligned16(dv, dtype)) {
+    const dim3 grid((unsigned)((int64_t)sh.B * (s_pad / misc::kDeltaTokens)));
     if (dtype == FA_DTYPE_BF16)
       misc::delta_token_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
           ov, dv, lse, delta, lse2, sh.S, sh.H, s_pad);
@@ -334,13 +391,26 @@ static int launch_rope_generic(int dtype_in, int dtype_out, const AttnShape& sh,
   const misc::TOut y2 = yb != nullptr ? *yb : y;
   const int64_t rows = (int64_t)sh.B * sh.S * sh.H;
   const bool token_path =
-      sh.D == 128 && (r.pos == nullptr || (r.axis_dim == 32 && r.n_axes == 4 && r.table != nullptr)) &&
+      sh.D == 128 && (r.pos == nullptr || (r.axis_dim == 32 && r.n_axes == 4)) &&
       aligned16(x, dtype_in) && aligned16(y, dtype_out) && aligned16(x2, dtype_in) &&
       aligned16(y2, dtype_out);
+  if (!token_path && r.table_out != nullptr) {
+    // only the token-major kernel writes the table as it goes: build it here
+    RopeArgs rt = r;
+    rt.table = nullptr;
+    const int64_t n = (int64_t)sh.S * rt.n_axes * (rt.axis_dim / 2);
+    misc::rope_table_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(rt, sh.S, r.table_out);
+    const int rc = launch_status();
+    if (rc != FA_OK) return rc;
+    RopeArgs rr = r;
+    rr.table = r.table_out;
+    rr.table_out = nullptr;
+    return launch_rope_generic(dtype_in, dtype_out, sh, x, y, rr, alpha, inverse, stream, xb, yb);
+  }
   if (token_path) {
     const dim3 grid((unsigned)((int64_t)sh.B * sh.S), npairs);
 #define FA_ROPE_T(TI, TO)                                                    \
-  misc::rope_token_kernel<TI, TO><<<grid, 256, 0, stream>>>(x, y, x2, y2, r, sh.S, \
+  misc::rope_token_kernel<TI, TO><<<grid, 32 * misc::kRopeWarps, 0, stream>>>(x, y, x2, y2, r, sh.S, \
                                                            sh.H, alpha, inverse)
     if (dtype_in == FA_DTYPE_BF16 && dtype_out == FA_DTYPE_BF16) FA_ROPE_T(__nv_bfloat16, __nv_bfloat16);
     else if (dtype_in == FA_DTYPE_F32 && dtype_out == FA_DTYPE_BF16) FA_ROPE_T(float, __nv_bfloat16);
@@ -399,9 +469,11 @@ int launch_rope(int dtype, const AttnShape& sh, const fa_tensor_t* x,
 int launch_rope_pair(int dtype, const AttnShape& sh, const fa_tensor_t* x0,
                      const fa_tensor_t* y0, const fa_tensor_t* x1,
                      const fa_tensor_t* y1, const fa_rope_t* rope, int inverse,
-                     int pos_offset, cudaStream_t stream, const float2* table) {
+                     int pos_offset, cudaStream_t stream, const float2* table,
+                     float2* table_out) {
   RopeArgs r = make_rope_args(rope, dtype == FA_DTYPE_BF16 ? 1 : 0, pos_offset);
   r.table = table;
+  r.table_out = table_out;
   const misc::TView xb = misc::tview(x1);
   const misc::TOut yb = misc::tout(y1);
   return launch_rope_generic(dtype, dtype, sh, misc::tview(x0), misc::tout(y0), r,

@@ -29,6 +29,9 @@ struct RopeArgs {
   // like pos (pos_offset applies), n_axes * axis_dim / 2 entries per token,
   // already rounded to the compute dtype. nullptr: evaluate from pos.
   const float2* table;
+  // Optional output: a rotation pass that evaluates (cos, sin) itself also
+  // writes them here in the table layout (for kernels that run after it).
+  float2* table_out;
   float inv_freq[kMaxRopeFreqs];  // theta^(-2j/dim_a), j < dim_a/2
 };
 
@@ -41,11 +44,10 @@ __device__ __forceinline__ float round_bf16_f(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));
 }
 
-// (cos, sin) of frequency f (axis f / half, index f % half) for `token`.
-__device__ __forceinline__ float2 rope_cs(const RopeArgs& r, int token, int f) {
+// (cos, sin) of frequency f (axis f / half, index f % half) for `token`,
+// evaluated from the positions (the table, if any, is not read).
+__device__ __forceinline__ float2 rope_cs_direct(const RopeArgs& r, int token, int f) {
   const int t = token + r.pos_offset;
-  const int nf = r.n_axes * (r.axis_dim >> 1);
-  if (r.table != nullptr) return r.table[(int64_t)t * nf + f];
   const int half = r.axis_dim >> 1;
   const float a = __fmul_rn(r.pos[(int64_t)t * r.n_axes + f / half], r.inv_freq[f]);
   float sn, cs;
@@ -55,6 +57,15 @@ __device__ __forceinline__ float2 rope_cs(const RopeArgs& r, int token, int f) {
     sn = round_bf16_f(sn);
   }
   return make_float2(cs, sn);
+}
+
+// The same, from the table when there is one.
+__device__ __forceinline__ float2 rope_cs(const RopeArgs& r, int token, int f) {
+  if (r.table != nullptr) {
+    const int nf = r.n_axes * (r.axis_dim >> 1);
+    return r.table[(int64_t)(token + r.pos_offset) * nf + f];
+  }
+  return rope_cs_direct(r, token, f);
 }
 
 // Rotates (inverse == false) or un-rotates one 128-wide row in place.
