@@ -100,6 +100,18 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map,
       : "memory");
 }
 
+// 4-D tiled store of a shared-memory tile into global memory (rows outside
+// the tensor are not written).
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map,
+                                             const void* src, int c0, int c1,
+                                             int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group "
+      "[%0, {%2, %3, %4, %5}], [%1];" ::"l"(reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
 // 4-D tiled reduce-add (fp32) of a shared-memory tile into global memory.
 __device__ __forceinline__ void tma_reduce_add_4d(const CUtensorMap* map,
                                                   const void* src, int c0,
