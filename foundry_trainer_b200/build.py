@@ -25,7 +25,7 @@ OBJ = ROOT / "_build"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + [
-    "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-rdc=true",
+    "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
     "--expt-relaxed-constexpr", "-I", str(ROOT / "include"), "-I", str(CSRC),
 ]
 
@@ -75,7 +75,7 @@ def _compile(src: Path, verbose_ptxas: bool) -> Path:
 
 def _link(objs: list[Path], out: Path) -> None:
     if _stale(out, objs):
-        _run([nvcc()] + ARCH + ["-shared", "-rdc=true", "-Xcompiler", "-fPIC"]
+        _run([nvcc()] + ARCH + ["-shared", "-Xcompiler", "-fPIC"]
              + [str(o) for o in objs] + ["-o", str(out)])
 
 

@@ -551,4 +551,6 @@ int launch_attn_bwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
   return launch_status();
 }
 
+int bwd_device_status() { return tu_device_status(); }
+
 }  // namespace fa

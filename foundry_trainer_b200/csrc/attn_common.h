@@ -102,4 +102,11 @@ int launch_lse_merge(int dtype, const AttnShape& sh, float* o_acc,
                      float* lse_acc, const fa_tensor_t* o_blk,
                      const float* lse_blk, int first, cudaStream_t stream);
 
+// Host: read-and-clear the device status word of each kernel translation
+// unit (0: no bounded wait expired; -1: unreadable).
+int fwd_device_status();
+int bwd_device_status();
+int f32_device_status();
+int misc_device_status();
+
 }  // namespace fa

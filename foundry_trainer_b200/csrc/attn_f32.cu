@@ -283,4 +283,6 @@ int launch_attn_bwd_f32(const AttnShape& sh, const fa_tensor_t* q,
   return launch_status();
 }
 
+int f32_device_status() { return tu_device_status(); }
+
 }  // namespace fa

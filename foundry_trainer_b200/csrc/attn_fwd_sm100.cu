@@ -275,6 +275,21 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
         m_use = m_cand;
         alpha = fast_exp2(m_run - m_cand);  // 0 when m_run == -inf
       }
+      // P = 2^(S*scale*log2e - m): packed bf16 pairs written over the
+      // registers already consumed; four partial sums
+      float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int i = 0; i < kKeys / 2; ++i) {
+        const float x0 = fmaf(sv[2 * i], sl2, -m_use);
+        const float x1 = fmaf(sv[2 * i + 1], sl2, -m_use);
+        const float p0 = ((2 * i) % kPolyEvery == kPolyEvery - 1) ? exp2_poly(x0) : fast_exp2(x0);
+        const float p1 = ((2 * i + 1) % kPolyEvery == kPolyEvery - 1) ? exp2_poly(x1) : fast_exp2(x1);
+        sum4[(2 * i) & 3] += p0;
+        sum4[(2 * i + 1) & 3] += p1;
+        sr[i] = pack_bf16(p0, p1);
+      }
+      tmem_st32(t_s + 0, sr);
+      tmem_st32(t_s + 32, sr + 32);
       // O_t may only be rescaled while no PV_t is in flight: after PV_t(j-1)
       // (already complete: S_t(j) was issued after it)
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
@@ -294,21 +309,6 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
           tmem_st16(t_o + cb * 16, orow);
         }
       }
-      // P = 2^(S*scale*log2e - m): packed bf16 pairs written over the
-      // registers already consumed; four partial sums
-      float sum4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int i = 0; i < kKeys / 2; ++i) {
-        const float x0 = fmaf(sv[2 * i], sl2, -m_use);
-        const float x1 = fmaf(sv[2 * i + 1], sl2, -m_use);
-        const float p0 = ((2 * i) % kPolyEvery == kPolyEvery - 1) ? exp2_poly(x0) : fast_exp2(x0);
-        const float p1 = ((2 * i + 1) % kPolyEvery == kPolyEvery - 1) ? exp2_poly(x1) : fast_exp2(x1);
-        sum4[(2 * i) & 3] += p0;
-        sum4[(2 * i + 1) & 3] += p1;
-        sr[i] = pack_bf16(p0, p1);
-      }
-      tmem_st32(t_s + 0, sr);
-      tmem_st32(t_s + 32, sr + 32);
       tmem_wait_st();
       l_run = l_run * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
       m_run = m_use;
@@ -399,5 +399,7 @@ int launch_attn_fwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
       tq, tk, tv, to, p);
   return launch_status();
 }
+
+int fwd_device_status() { return tu_device_status(); }
 
 }  // namespace fa

@@ -17,7 +17,6 @@
 
 namespace fa {
 
-__device__ int g_device_status = 0;
 
 // ------------------------------------------------------------ TMA encoding
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
@@ -252,13 +251,14 @@ const char* fa_build_info(void) {
 
 int fa_device_status(void) {
   if (cudaDeviceSynchronize() != cudaSuccess) return FA_ERR_LAUNCH;
-  int v = 0;
-  if (cudaMemcpyFromSymbol(&v, g_device_status, sizeof(int)) != cudaSuccess)
-    return FA_ERR_LAUNCH;
-  const int zero = 0;
-  if (v != 0 && cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int)) != cudaSuccess)
-    return FA_ERR_LAUNCH;
-  return v;
+  // every translation unit's word is read (and cleared); the first code wins
+  int first = 0;
+  for (int v : {fwd_device_status(), bwd_device_status(), f32_device_status(),
+                misc_device_status()}) {
+    if (v < 0) return FA_ERR_LAUNCH;
+    if (first == 0) first = v;
+  }
+  return first;
 }
 
 size_t fa_fwd_workspace_bytes(int dtype, int B, int S, int H, int D,

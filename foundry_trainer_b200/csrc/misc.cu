@@ -522,4 +522,6 @@ int launch_lse_merge(int dtype, const AttnShape& sh, float* o_acc,
   return launch_status();
 }
 
+int misc_device_status() { return tu_device_status(); }
+
 }  // namespace fa

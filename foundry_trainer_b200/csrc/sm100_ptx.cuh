@@ -15,11 +15,25 @@
 namespace fa {
 
 // ---------------------------------------------------------------- status word
-// One int per device, set by kernels when a bounded wait expires.
-extern __device__ int g_device_status;
+// Set by kernels when a bounded wait expires. The library is compiled one
+// translation unit at a time (no relocatable device code, so that register
+// reallocation with setmaxnreg is honoured): every unit that launches kernels
+// has its own word and reads it back with tu_device_status().
+static __device__ int g_device_status = 0;
 
 __device__ __forceinline__ void report_status(int code) {
   atomicCAS(&g_device_status, 0, code);
+}
+
+// Host: this translation unit's status word (cleared when non-zero), or -1
+// when it cannot be read.
+static inline int tu_device_status() {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_device_status, sizeof(int)) != cudaSuccess) return -1;
+  const int zero = 0;
+  if (v != 0 && cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int)) != cudaSuccess)
+    return -1;
+  return v;
 }
 
 // Cycles a single wait may spin before giving up (~1 s at 1.9 GHz).

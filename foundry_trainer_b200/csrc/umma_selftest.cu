@@ -12,10 +12,6 @@
 
 #include "sm100_ptx.cuh"
 
-namespace fa {
-__device__ int g_device_status = 0;
-}
-
 namespace {
 
 using namespace fa;
