@@ -176,11 +176,12 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
       constexpr uint32_t kIdescO = idesc_bf16(128, 128, false, true);
       bool ok = mbar_wait(&bars[B_Q], 0);
       tc_fence_after();
-      // S_t(j) = Q_t K_j^T. S_t is free once PV_t(j-1) has read P_t(j-1).
+      // S_t(j) = Q_t K_j^T. It overwrites P_t(j-1), which PV_t(j-1) reads:
+      // tcgen05.mma operations issued by one thread execute in issue order,
+      // so S_t(j) is issued right behind PV_t(j-1) without waiting for it.
       auto issue_s = [&](int t, int j) -> bool {
         const int s = j % kKStages, n = j / kKStages;
         if (t == 0 && !mbar_wait(&bars[B_KFULL + s], n & 1)) return false;
-        if (j > 0 && !mbar_wait(&bars[B_PVDONE + t], (j - 1) & 1)) return false;
         tc_fence_after();
         const uint32_t q_base = smem_u32(smem + kOffQ + t * kTileBytes);
         const uint32_t k_base = smem_u32(smem + kOffK + s * kTileBytes);

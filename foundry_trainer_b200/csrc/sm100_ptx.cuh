@@ -81,6 +81,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr,
   return ok != 0;
 }
 
+// Non-blocking: true when the phase with the given parity has completed.
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Waits until the phase with the given parity has completed. Returns false
 // (and records the timeout) when the budget runs out.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
