@@ -15,7 +15,8 @@
 // CTAs of one head add into different dQ rows at any moment instead of all
 // contending for the same L2 lines. 14 warps:
 //   warp 8        TMA producer: K, V once; Q_i, dO_i, LSE_i, Delta_i per step
-//   warp 9        tcgen05 MMA issuer, TMEM owner
+//   warp 9        tcgen05 MMA issuer (the whole warp runs the loop, one
+//                 elected lane issues), TMEM owner
 //   warps 0-3     softmax backward for queries 0-63 of the tile (one key row
 //                 per thread); dV epilogue
 //   warps 10-13   the same for queries 64-127; dK epilogue
@@ -31,8 +32,10 @@
 //   B [128,256)  dP^T_i, then dQ^T_i = K^T dS^T_i (fp32; lane = head-dim
 //                column, column = query)
 //   dV [256,384) dK [384,512)   accumulators over all Q tiles
-// Every MMA that overwrites columns another MMA reads waits for that MMA's
-// commit first; dQ_i is drained while S^T_{i+1} runs, and TMEM B is handed
+// tcgen05.mma operations issued by one thread execute in issue order, so an
+// MMA that overwrites columns an earlier MMA reads needs no wait; TMEM read by
+// the softmax or the drain is handed back through barriers. dQ_i is drained
+// while S^T_{i+1} runs, and TMEM B is handed
 // back (DQFREE) as soon as it has been read into registers. The dS^T tile is
 // free for the next step's softmax once the dQ^T MMA has read it (DSFREE).
 #include "attn_common.h"
@@ -68,7 +71,6 @@ constexpr int B_SDP = 5;
 constexpr int B_PS = 6;
 constexpr int B_DQFULL = 7;
 constexpr int B_DQFREE = 8;
-constexpr int B_DVK = 9;
 constexpr int B_FINAL = 10;
 constexpr int B_DSFREE = 11;
 
@@ -217,7 +219,6 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
     mbar_init(&bars[B_PS], 256);
     mbar_init(&bars[B_DQFULL], 1);
     mbar_init(&bars[B_DQFREE], 128);
-    mbar_init(&bars[B_DVK], 1);
     mbar_init(&bars[B_FINAL], 1);
     mbar_init(&bars[B_DSFREE], 1);
     *abort_flag = 0;
@@ -269,63 +270,62 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
       if (!ok) *abort_flag = 1;
     }
   } else if (warp == 9) {
-    // ----------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    // ---------------------------------------- MMA issuer (whole warp, one lane issues)
+    {
       constexpr uint32_t kIdKK = idesc_bf16(128, 128, false, false);
       constexpr uint32_t kIdKM = idesc_bf16(128, 128, false, true);
       constexpr uint32_t kIdMM = idesc_bf16(128, 128, true, true);
       const uint32_t k_base = smem_u32(smem + kOffK);
       const uint32_t v_base = smem_u32(smem + kOffV);
       const uint32_t ds_base = smem_u32(smem + kOffDS);
-      bool ok = mbar_wait(&bars[B_KV], 0);
+      bool ok = mbar_wait_w(&bars[B_KV], 0);
       tc_fence_after();
       for (int i = 0; ok && i < nq; ++i) {
         const int st = i & 1, n = i >> 1;
-        if (*abort_flag) { ok = false; break; }
-        if (!(ok = mbar_wait(&bars[B_QFULL + st], n & 1))) break;
+        if (__any_sync(0xffffffffu, *abort_flag != 0)) { ok = false; break; }
+        if (!(ok = mbar_wait_w(&bars[B_QFULL + st], n & 1))) break;
         const uint32_t q_base = smem_u32(smem + kOffStage + st * kStageBytes);
         const uint32_t do_base = q_base + kTileBytes;
-        // S^T_i = K Q_i^T -> A   (A was read by dV/dK of step i-1)
-        if (i > 0 && !(ok = mbar_wait(&bars[B_DVK], (i - 1) & 1))) break;
+        // S^T_i = K Q_i^T -> A. A was read by dV/dK of step i-1: tcgen05.mma
+        // operations issued by one thread execute in issue order, so no wait.
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          umma_ss(tmem + kColA, kmajor_desc(k_base, kk, kBlkBytes),
-                  kmajor_desc(q_base, kk, kBlkBytes), kIdKK, kk > 0);
-        // dP^T_i = V dO_i^T -> B   (B held dQ_{i-1} until it was drained)
-        if (i > 0 && !(ok = mbar_wait(&bars[B_DQFREE], (i - 1) & 1))) break;
+          umma_ss_w(tmem + kColA, kmajor_desc(k_base, kk, kBlkBytes),
+                    kmajor_desc(q_base, kk, kBlkBytes), kIdKK, kk > 0);
+        // dP^T_i = V dO_i^T -> B   (B held dQ_{i-1} until the drain read it)
+        if (i > 0 && !(ok = mbar_wait_w(&bars[B_DQFREE], (i - 1) & 1))) break;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          umma_ss(tmem + kColB, kmajor_desc(v_base, kk, kBlkBytes),
-                  kmajor_desc(do_base, kk, kBlkBytes), kIdKK, kk > 0);
-        umma_commit(&bars[B_SDP]);
-        if (!(ok = mbar_wait(&bars[B_PS], i & 1))) break;
+          umma_ss_w(tmem + kColB, kmajor_desc(v_base, kk, kBlkBytes),
+                    kmajor_desc(do_base, kk, kBlkBytes), kIdKK, kk > 0);
+        umma_commit_w(&bars[B_SDP]);
+        if (!(ok = mbar_wait_w(&bars[B_PS], i & 1))) break;
         tc_fence_after();
         // dV += P^T dO_i ; dK += dS^T Q_i   (A operands from TMEM; K slice kk
         // is queries 16kk..16kk+15: half kk>>2, eight packed columns each)
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          umma_ts(tmem + kColDV, tmem + kColA + (kk >> 2) * 64 + (kk & 3) * 8,
-                  mnmajor_desc(do_base, kk, kBlkBytes), kIdKM,
-                  (i > 0 || kk > 0) ? 1u : 0u);
+          umma_ts_w(tmem + kColDV, tmem + kColA + (kk >> 2) * 64 + (kk & 3) * 8,
+                    mnmajor_desc(do_base, kk, kBlkBytes), kIdKM,
+                    (i > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          umma_ts(tmem + kColDK,
-                  tmem + kColA + (kk >> 2) * 64 + 32 + (kk & 3) * 8,
-                  mnmajor_desc(q_base, kk, kBlkBytes), kIdKM,
-                  (i > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&bars[B_DVK]);
+          umma_ts_w(tmem + kColDK,
+                    tmem + kColA + (kk >> 2) * 64 + 32 + (kk & 3) * 8,
+                    mnmajor_desc(q_base, kk, kBlkBytes), kIdKM,
+                    (i > 0 || kk > 0) ? 1u : 0u);
         // dQ^T_i = K^T dS^T_i -> B   (both operands MN-major in shared memory)
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          umma_ss(tmem + kColB, mnmajor_desc(k_base, kk, kBlkBytes),
-                  mnmajor_desc(ds_base, kk, kBlkBytes), kIdMM, kk > 0);
-        umma_commit(&bars[B_DQFULL]);
-        umma_commit(&bars[B_DSFREE]);
+          umma_ss_w(tmem + kColB, mnmajor_desc(k_base, kk, kBlkBytes),
+                    mnmajor_desc(ds_base, kk, kBlkBytes), kIdMM, kk > 0);
+        umma_commit_w(&bars[B_DQFULL]);
+        umma_commit_w(&bars[B_DSFREE]);
       }
-      if (!ok) *abort_flag = 1;
-      umma_commit(&bars[B_FINAL]);
+      if (!ok && lane == 0) *abort_flag = 1;
+      umma_commit_w(&bars[B_FINAL]);
       mbar_wait(&bars[B_FINAL], 0);
     }
   } else if (warp < 4 || warp >= 10) {

@@ -9,16 +9,20 @@
 // end (both are one bf16 rounding of P; the LSE itself is fp32).
 //
 // One CTA owns two 128-row Q tiles (256 query rows) of one (b, h) and streams
-// 128-key K/V tiles through TMA rings, so every K/V tile brought into shared
-// memory feeds two tiles of tensor-core work. The CTAs of a head start at
+// 128-key K and V tiles through one TMA ring of five slots, in the order they
+// are consumed (K_j, V_j, K_{j+1}, ...), so every K/V tile brought into shared
+// memory feeds two tiles of tensor-core work and a V tile is requested about
+// two steps before its first use (the loads share shared-memory bandwidth
+// with the tensor core and take several microseconds to land). The CTAs of a head start at
 // different K/V tiles and wrap (the online softmax is order-independent), so
 // they do not all request the same tile from L2 at once.
 //   warps 0-3   softmax of Q tile 0: one thread per row, the whole 128-key
 //               row of S in registers; O rescale (rare) and the epilogue
 //   warps 4-7   the same for Q tile 1
-//   warp 8      TMA producer of Q0, Q1 and K (one lane)
-//   warp 10     TMA producer of V (one lane)
-//   warp 9      tcgen05 MMA issuer (one lane), TMEM owner
+//   warp 8      TMA producer of Q0, Q1, K and V (one lane)
+//   warp 9      tcgen05 MMA issuer (the whole warp runs the loop, one
+//               elected lane issues), TMEM owner
+//   warp 10     idle
 // TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512).
 // P_t (bf16, two per column) is written over the first 64 columns of S_t
 // once the row of S_t is in registers; it is the TMEM A operand of
@@ -36,25 +40,21 @@ constexpr int kTiles = 2;           // Q tiles per CTA
 constexpr int kKeys = 128;          // keys per K/V tile
 constexpr int kTileBytes = 32768;   // 128 x 128 bf16
 constexpr int kBlkBytes = 16384;    // one 64-column swizzle block
-constexpr int kKStages = 3;
-constexpr int kVStages = 2;
+constexpr int kSlots = 5;           // K/V ring: load n (K_j: n = 2j, V_j: 2j+1) in slot n % 5
 constexpr int kThreads = 352;
 
 // shared memory map (offsets from a 1024-byte aligned base)
 constexpr int kOffQ = 0;  // Q0, Q1; each becomes its tile's O staging at the end
-constexpr int kOffK = kOffQ + kTiles * kTileBytes;
-constexpr int kOffV = kOffK + kKStages * kTileBytes;
-constexpr int kOffBar = kOffV + kVStages * kTileBytes;
+constexpr int kOffKV = kOffQ + kTiles * kTileBytes;
+constexpr int kOffBar = kOffKV + kSlots * kTileBytes;
 constexpr int kNumBars = 24;
 constexpr int kOffMisc = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffMisc + 64 + 1024;  // + alignment slack
 
 // barrier indices
 constexpr int B_Q = 0;
-constexpr int B_KFULL = 1;    // + stage (3)
-constexpr int B_KEMPTY = 4;   // + stage (3)
-constexpr int B_VFULL = 7;    // + stage (2)
-constexpr int B_VEMPTY = 9;   // + stage (2)
+constexpr int B_FULL = 1;     // + slot (5)
+constexpr int B_EMPTY = 6;    // + slot (5)
 constexpr int B_SFULL = 11;   // + tile: S_t(j) complete
 constexpr int B_PREADY = 13;  // + tile: softmax wrote P_t(j) (and rescaled O_t)
 constexpr int B_PVDONE = 15;  // + tile: O_t += P_t(j) V_j completed
@@ -101,13 +101,9 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
 
   if (threadIdx.x == 0) {
     mbar_init(&bars[B_Q], 1);
-    for (int s = 0; s < kKStages; ++s) {
-      mbar_init(&bars[B_KFULL + s], 1);
-      mbar_init(&bars[B_KEMPTY + s], 1);
-    }
-    for (int s = 0; s < kVStages; ++s) {
-      mbar_init(&bars[B_VFULL + s], 1);
-      mbar_init(&bars[B_VEMPTY + s], 1);
+    for (int s = 0; s < kSlots; ++s) {
+      mbar_init(&bars[B_FULL + s], 1);
+      mbar_init(&bars[B_EMPTY + s], 1);
     }
     for (int t = 0; t < kTiles; ++t) {
       mbar_init(&bars[B_SFULL + t], 1);
@@ -128,10 +124,11 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 8) {
-    // ----------------------------------------------- producer: Q0, Q1 and K
+    // ------------------------------------------------ producer: Q0, Q1, K, V
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
       const int row = pair * kTiles * kRows;
       mbar_arrive_expect_tx(&bars[B_Q], kTiles * kTileBytes);
       for (int t = 0; t < kTiles; ++t) {
@@ -140,92 +137,76 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
         tma_load_4d(d + kBlkBytes, &tm_q, &bars[B_Q], 64, row + t * kRows, h, b);
       }
       bool ok = true;
-      for (int jk = 0; jk < nkv; ++jk) {
+      for (int n = 0; n < 2 * nkv; ++n) {
         if (*abort_flag) break;
-        const int s = jk % kKStages, n = jk / kKStages;
-        if (jk >= kKStages && !(ok = mbar_wait(&bars[B_KEMPTY + s], (n - 1) & 1))) break;
-        uint8_t* d = smem + kOffK + s * kTileBytes;
-        mbar_arrive_expect_tx(&bars[B_KFULL + s], kTileBytes);
-        const int krow = kv_tile_of(jk, pair, nkv) * kKeys;
-        tma_load_4d(d, &tm_k, &bars[B_KFULL + s], 0, krow, h, b);
-        tma_load_4d(d + kBlkBytes, &tm_k, &bars[B_KFULL + s], 64, krow, h, b);
-      }
-      if (!ok) *abort_flag = 1;
-    }
-  } else if (warp == 10) {
-    // ------------------------------------------------------- producer: V
-    if (lane == 0) {
-      tma_prefetch_desc(&tm_v);
-      bool ok = true;
-      for (int jv = 0; jv < nkv; ++jv) {
-        if (*abort_flag) break;
-        const int s = jv % kVStages, n = jv / kVStages;
-        if (jv >= kVStages && !(ok = mbar_wait(&bars[B_VEMPTY + s], (n - 1) & 1))) break;
-        uint8_t* d = smem + kOffV + s * kTileBytes;
-        mbar_arrive_expect_tx(&bars[B_VFULL + s], kTileBytes);
-        const int vrow = kv_tile_of(jv, pair, nkv) * kKeys;
-        tma_load_4d(d, &tm_v, &bars[B_VFULL + s], 0, vrow, h, b);
-        tma_load_4d(d + kBlkBytes, &tm_v, &bars[B_VFULL + s], 64, vrow, h, b);
+        const int s = n % kSlots, u = n / kSlots;
+        if (n >= kSlots && !(ok = mbar_wait(&bars[B_EMPTY + s], (u - 1) & 1))) break;
+        uint8_t* d = smem + kOffKV + s * kTileBytes;
+        const CUtensorMap* tm = (n & 1) ? &tm_v : &tm_k;
+        mbar_arrive_expect_tx(&bars[B_FULL + s], kTileBytes);
+        const int kvrow = kv_tile_of(n >> 1, pair, nkv) * kKeys;
+        tma_load_4d(d, tm, &bars[B_FULL + s], 0, kvrow, h, b);
+        tma_load_4d(d + kBlkBytes, tm, &bars[B_FULL + s], 64, kvrow, h, b);
       }
       if (!ok) *abort_flag = 1;
     }
   } else if (warp == 9) {
-    // ----------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    // ---------------------------------------- MMA issuer (whole warp, one lane issues)
+    {
       constexpr uint32_t kIdescS = idesc_bf16(128, 128, false, false);
       constexpr uint32_t kIdescO = idesc_bf16(128, 128, false, true);
-      bool ok = mbar_wait(&bars[B_Q], 0);
+      bool ok = mbar_wait_w(&bars[B_Q], 0);
       tc_fence_after();
       // S_t(j) = Q_t K_j^T. It overwrites P_t(j-1), which PV_t(j-1) reads:
       // tcgen05.mma operations issued by one thread execute in issue order,
       // so S_t(j) is issued right behind PV_t(j-1) without waiting for it.
       auto issue_s = [&](int t, int j) -> bool {
-        const int s = j % kKStages, n = j / kKStages;
-        if (t == 0 && !mbar_wait(&bars[B_KFULL + s], n & 1)) return false;
+        const int s = (2 * j) % kSlots, u = (2 * j) / kSlots;
+        if (t == 0 && !mbar_wait_w(&bars[B_FULL + s], u & 1)) return false;
         tc_fence_after();
         const uint32_t q_base = smem_u32(smem + kOffQ + t * kTileBytes);
-        const uint32_t k_base = smem_u32(smem + kOffK + s * kTileBytes);
+        const uint32_t k_base = smem_u32(smem + kOffKV + s * kTileBytes);
         const uint32_t d = tmem + kColS + (uint32_t)t * 128u;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          umma_ss(d, kmajor_desc(q_base, kk, kBlkBytes),
-                  kmajor_desc(k_base, kk, kBlkBytes), kIdescS, kk > 0);
-        umma_commit(&bars[B_SFULL + t]);
-        if (t == kTiles - 1) umma_commit(&bars[B_KEMPTY + s]);
+          umma_ss_w(d, kmajor_desc(q_base, kk, kBlkBytes),
+                    kmajor_desc(k_base, kk, kBlkBytes), kIdescS, kk > 0);
+        umma_commit_w(&bars[B_SFULL + t]);
+        if (t == kTiles - 1) umma_commit_w(&bars[B_EMPTY + s]);
         return true;
       };
       // O_t += P_t(j) V_j
       auto issue_pv = [&](int t, int j) -> bool {
-        const int s = j % kVStages, n = j / kVStages;
-        if (t == 0 && !mbar_wait(&bars[B_VFULL + s], n & 1)) return false;
-        if (!mbar_wait(&bars[B_PREADY + t], j & 1)) return false;
+        const int s = (2 * j + 1) % kSlots, u = (2 * j + 1) / kSlots;
+        if (t == 0 && !mbar_wait_w(&bars[B_FULL + s], u & 1)) return false;
+        if (!mbar_wait_w(&bars[B_PREADY + t], j & 1)) return false;
         tc_fence_after();
-        const uint32_t v_base = smem_u32(smem + kOffV + s * kTileBytes);
+        const uint32_t v_base = smem_u32(smem + kOffKV + s * kTileBytes);
         const uint32_t p_col = tmem + kColS + (uint32_t)t * 128u;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          umma_ts(tmem + kColO + (uint32_t)t * 128u, p_col + kk * 8,
-                  mnmajor_desc(v_base, kk, kBlkBytes), kIdescO,
-                  (j > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&bars[B_PVDONE + t]);
-        if (t == kTiles - 1) umma_commit(&bars[B_VEMPTY + s]);
+          umma_ts_w(tmem + kColO + (uint32_t)t * 128u, p_col + kk * 8,
+                    mnmajor_desc(v_base, kk, kBlkBytes), kIdescO,
+                    (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit_w(&bars[B_PVDONE + t]);
+        if (t == kTiles - 1) umma_commit_w(&bars[B_EMPTY + s]);
         return true;
       };
       if (ok) ok = issue_s(0, 0);
       if (ok) ok = issue_s(1, 0);
       for (int j = 0; ok && j < nkv; ++j) {
-        if (*abort_flag) { ok = false; break; }
+        if (__any_sync(0xffffffffu, *abort_flag != 0)) { ok = false; break; }
         for (int t = 0; ok && t < kTiles; ++t) {
           ok = issue_pv(t, j);
           if (ok && j + 1 < nkv) ok = issue_s(t, j + 1);
         }
       }
-      if (!ok) *abort_flag = 1;
+      if (!ok && lane == 0) *abort_flag = 1;
       // drain: every MMA issued above completes before TMEM is released
-      umma_commit(&bars[B_FINAL]);
+      umma_commit_w(&bars[B_FINAL]);
       mbar_wait(&bars[B_FINAL], 0);
     }
-  } else {
+  } else if (warp < 8) {
     // ------------------------------------------------------------- softmax
     const int t = warp >> 2;                  // Q tile of this warpgroup
     const int sub = warp & 3;                 // TMEM lane quarter

@@ -412,6 +412,26 @@ __device__ __forceinline__ bool elect_one() {
   return pred != 0;
 }
 
+// Warp-wide forms for the MMA-issuing warp: the whole (converged) warp runs
+// the issue loop, so descriptors and addresses are warp-uniform values, and
+// one elected lane issues. A loop run by a single lane pays extra issue
+// latency per tcgen05.mma when its operands change from one call to the next.
+__device__ __forceinline__ void umma_ss_w(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  if (elect_one()) umma_ss(d_tmem, a_desc, b_desc, idesc, accumulate);
+}
+__device__ __forceinline__ void umma_ts_w(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  if (elect_one()) umma_ts(d_tmem, a_tmem, b_desc, idesc, accumulate);
+}
+__device__ __forceinline__ void umma_commit_w(uint64_t* bar) {
+  if (elect_one()) umma_commit(bar);
+}
+// Bounded wait whose result is the same in every lane of the warp.
+__device__ __forceinline__ bool mbar_wait_w(uint64_t* bar, uint32_t parity) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity));
+}
+
 // Named barrier over `nthreads` threads that also ORs a predicate across
 // them: every participant gets the same answer, so a group can leave a loop
 // together (no participant is left waiting at a later named barrier).
