@@ -73,6 +73,7 @@ constexpr int B_DQFULL = 7;
 constexpr int B_DQFREE = 8;
 constexpr int B_FINAL = 10;
 constexpr int B_DSFREE = 11;
+constexpr int B_DSREADY = 12;  // dS^T_i copied to shared memory (drain warps)
 
 constexpr uint32_t kColA = 0;
 constexpr uint32_t kColB = 128;
@@ -221,6 +222,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
     mbar_init(&bars[B_DQFREE], 128);
     mbar_init(&bars[B_FINAL], 1);
     mbar_init(&bars[B_DSFREE], 1);
+    mbar_init(&bars[B_DSREADY], 128);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -316,7 +318,10 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                     tmem + kColA + (kk >> 2) * 64 + 32 + (kk & 3) * 8,
                     mnmajor_desc(q_base, kk, kBlkBytes), kIdKM,
                     (i > 0 || kk > 0) ? 1u : 0u);
-        // dQ^T_i = K^T dS^T_i -> B   (both operands MN-major in shared memory)
+        // dQ^T_i = K^T dS^T_i -> B   (both operands MN-major in shared memory;
+        // dS^T_i reaches shared memory while dV/dK run)
+        if (!(ok = mbar_wait_w(&bars[B_DSREADY], i & 1))) break;
+        tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
           umma_ss_w(tmem + kColB, mnmajor_desc(k_base, kk, kBlkBytes),
@@ -336,7 +341,6 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
     const uint32_t lane_off = (uint32_t)(sub * 32) << 16;
     const uint32_t t_a = tmem + lane_off + kColA + (uint32_t)half * 64u;
     const uint32_t t_b = tmem + lane_off + kColB + (uint32_t)half * 64u;
-    uint8_t* ds_blk = smem + kOffDS + half * kBlkBytes;
     const float sl2 = p.scale_log2;
     bool ok = true;
     for (int i = 0; i < nq; ++i) {
@@ -386,23 +390,6 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
         tmem_st8(t_a + 32 + cb * 8, dk);  // dS^T: columns 64h + [32, 64)
       }
       tmem_wait_st();
-      // dS^T also goes to shared memory (B operand of dQ^T), once the dQ^T
-      // MMA of step i-1 has read the tile: read back this half's 32 packed
-      // columns and store them as 16-byte chunks 0-7 of swizzle block h.
-      if (i > 0) {
-        ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_DSFREE], (i - 1) & 1));
-        if (!ok) break;
-      }
-      {
-        uint32_t dsr[32];
-        tmem_ld32(t_a + 32, dsr);
-        tmem_wait_ld();
-#pragma unroll
-        for (int u = 0; u < 8; ++u)
-          *reinterpret_cast<uint4*>(ds_blk + sw128_offset(key_in_tile, u)) =
-              make_uint4(dsr[4 * u], dsr[4 * u + 1], dsr[4 * u + 2], dsr[4 * u + 3]);
-      }
-      fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&bars[B_PS]);
     }
@@ -454,7 +441,42 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
 #pragma unroll
       for (int j = 0; j < 64; ++j) buf[j * 128 + d] = __uint_as_float(v[j]);
     };
+    // dS^T copy: this thread's key row (lane quarter of the warp), both query
+    // halves: 32 packed columns each, stored as 16-byte chunks 0-7 of swizzle
+    // block h (the MN-major B operand of the dQ^T MMA)
+    const uint32_t t_ds = tmem + lane_off + kColA + 32;
+    const int key_row = sub * 32 + lane;
+    int reduce_pending = -1;  // slot whose bulk reduces the leader has not yet seen read
     for (int i = 0; i < nq; ++i) {
+      // dS^T_i: the softmax wrote it to TMEM (PS); the dQ^T MMA of step i-1
+      // has finished reading the shared tile (DSFREE)
+      {
+        bool stop = *abort_flag != 0;
+        if (!stop) stop = !mbar_wait(&bars[B_PS], i & 1);
+        if (!stop && i > 0) stop = !mbar_wait(&bars[B_DSFREE], (i - 1) & 1);
+        if (named_bar_any(2, 128, stop)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t dsr[32];
+          tmem_ld32(t_ds + hh * 64, dsr);
+          tmem_wait_ld();
+          uint8_t* blk = smem + kOffDS + hh * kBlkBytes;
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            *reinterpret_cast<uint4*>(blk + sw128_offset(key_row, u)) =
+                make_uint4(dsr[4 * u], dsr[4 * u + 1], dsr[4 * u + 2], dsr[4 * u + 3]);
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(&bars[B_DSREADY]);
+      }
+      // the previous step's reduces have had a whole dS copy to read their slot
+      if (leader && reduce_pending >= 0) {
+        bulk_wait_group_read0();
+        mbar_arrive(&bars[B_QEMPTY + reduce_pending]);
+        reduce_pending = -1;
+      }
       // leave together: the staging uses a named barrier over warps 4-7
       bool stop = *abort_flag != 0;
       if (!stop) stop = !mbar_wait(&bars[B_DQFULL], i & 1);
@@ -482,9 +504,12 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
         bulk_reduce_add_f32(dst, buf, 32768);
         bulk_reduce_add_f32(dst + 64 * 128, buf + 64 * 128, 32768);
         bulk_commit_group();
-        bulk_wait_group_read0();
-        mbar_arrive(&bars[B_QEMPTY + st]);  // the producer may reload the slot
+        reduce_pending = st;  // slot handed back once the reduces have read it
       }
+    }
+    if (leader && reduce_pending >= 0) {
+      bulk_wait_group_read0();
+      mbar_arrive(&bars[B_QEMPTY + reduce_pending]);
     }
     if (leader) bulk_wait_group0();  // reductions complete before exit
   }
