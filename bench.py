@@ -1,13 +1,16 @@
 """Benchmark of the joint-attention forward + backward on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c4|c5] [--impl ours|reference]
+                    [--ncu-case]
 
 A step is one forward + backward of the op (axial RoPE inside) over one
 synthetic batch of the named configuration, inputs resident in HBM. With N > 1
 (launched under torch.distributed.run, one rank per GPU) every rank runs its
 own batch x head partition of the workload with no collective on the data
 path (weak scaling); the timed region is bracketed by a barrier and a device
-synchronise, and the maximum time over ranks is reported.
+synchronise, and the maximum time over ranks is reported. `--config c5` runs
+the long-sequence case as a ring instead: one sequence of 16896 rows sharded
+over the ranks, K/V passed round an NCCL ring (strong scaling).
 
 Rank 0 prints one JSON line: the metric (TFLOP/s, FlashAttention accounting
 14*B*H*S^2*D), the roofline of the dominant kernel (the backward kernel,
