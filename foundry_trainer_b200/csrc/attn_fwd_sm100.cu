@@ -64,8 +64,13 @@ constexpr uint32_t kColS = 0;    // + 128 t
 constexpr uint32_t kColO = 256;  // + 128 t
 
 // Fraction of the exponentials evaluated on the FMA pipe (polynomial)
-// instead of MUFU: columns c with (c % kPolyEvery) == kPolyEvery - 1.
-constexpr int kPolyEvery = 8;
+// instead of MUFU: columns c with (c % kPolyEvery) == kPolyEvery - 1; 0 = none.
+// Measured at C2: none 224.7 us, one in eight 235.6 us, one in four 240 us —
+// the softmax is bound by instruction issue and latency, not by MUFU.
+constexpr int kPolyEvery = 0;
+__device__ __forceinline__ constexpr bool poly_column(int c) {
+  return kPolyEvery > 0 && c % (kPolyEvery > 0 ? kPolyEvery : 1) == kPolyEvery - 1;
+}
 
 // K/V tile visited at step j by the CTA with tile pair `pair`.
 __device__ __forceinline__ int kv_tile_of(int j, int pair, int nkv) {
@@ -237,16 +242,14 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
         for (int c = 0; c < kKeys; ++c)
           if (c >= valid) sv[c] = -INFINITY;
       }
-      // row maximum: four independent chains, then combine
+      // row maximum: four independent chains of three-input maxima
       float m4[4] = {sv[0], sv[1], sv[2], sv[3]};
 #pragma unroll
-      for (int c = 4; c < kKeys; c += 4) {
-        m4[0] = fmaxf(m4[0], sv[c + 0]);
-        m4[1] = fmaxf(m4[1], sv[c + 1]);
-        m4[2] = fmaxf(m4[2], sv[c + 2]);
-        m4[3] = fmaxf(m4[3], sv[c + 3]);
+      for (int c = 4; c < kKeys; c += 8) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) m4[k] = fmax3(m4[k], sv[c + 2 * k], sv[c + 2 * k + 1]);
       }
-      const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+      const float mx = fmax3(fmaxf(m4[0], m4[1]), m4[2], m4[3]);
       const float m_cand = mx * sl2;
       float m_use = m_run;
       float alpha = 1.f;
@@ -259,17 +262,21 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
       }
       // P = 2^(S*scale*log2e - m): packed bf16 pairs written over the
       // registers already consumed; four partial sums
-      float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+      // (pairs of columns through the packed fp32x2 FMA / add)
+      const uint64_t sl2_2 = f2_pack(sl2, sl2), negm_2 = f2_pack(-m_use, -m_use);
+      uint64_t sum2[2] = {0ull, 0ull};
 #pragma unroll
       for (int i = 0; i < kKeys / 2; ++i) {
-        const float x0 = fmaf(sv[2 * i], sl2, -m_use);
-        const float x1 = fmaf(sv[2 * i + 1], sl2, -m_use);
-        const float p0 = ((2 * i) % kPolyEvery == kPolyEvery - 1) ? exp2_poly(x0) : fast_exp2(x0);
-        const float p1 = ((2 * i + 1) % kPolyEvery == kPolyEvery - 1) ? exp2_poly(x1) : fast_exp2(x1);
-        sum4[(2 * i) & 3] += p0;
-        sum4[(2 * i + 1) & 3] += p1;
+        float x0, x1;
+        f2_unpack(ffma2(f2_pack(sv[2 * i], sv[2 * i + 1]), sl2_2, negm_2), x0, x1);
+        const float p0 = poly_column(2 * i) ? exp2_poly(x0) : fast_exp2(x0);
+        const float p1 = poly_column(2 * i + 1) ? exp2_poly(x1) : fast_exp2(x1);
+        sum2[i & 1] = fadd2(sum2[i & 1], f2_pack(p0, p1));
         sr[i] = pack_bf16(p0, p1);
       }
+      float sum4[4];
+      f2_unpack(sum2[0], sum4[0], sum4[1]);
+      f2_unpack(sum2[1], sum4[2], sum4[3]);
       tmem_st32(t_s + 0, sr);
       tmem_st32(t_s + 32, sr + 32);
       // O_t may only be rescaled while no PV_t is in flight: after PV_t(j-1)
