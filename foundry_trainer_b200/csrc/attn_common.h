@@ -74,9 +74,11 @@ int launch_attn_bwd_f32(const AttnShape& sh, const fa_tensor_t* q,
 // elementwise helpers (misc.cu)
 // delta[b,h,s] = sum_d dO*O over rows s < s_pad (0 for s >= S); when lse2 is
 // non-null also lse2[b,h,s] = lse*log2(e) (+inf for s >= S).
+// zero_acc: an fp32 (B, H, s_pad, D) buffer cleared on the way (or nullptr)
 int launch_bwd_delta(int dtype, const AttnShape& sh, const fa_tensor_t* o,
                      const fa_tensor_t* d_o, const float* lse, float* delta,
-                     float* lse2, int s_pad, cudaStream_t stream);
+                     float* lse2, int s_pad, cudaStream_t stream,
+                     float* zero_acc = nullptr);
 // (cos, sin) table for tokens [0, S) (+pos_offset), S * n_axes*axis_dim/2 float2
 int launch_rope_table(int dtype, int S, const fa_rope_t* rope, int pos_offset,
                       float2* table, cudaStream_t stream);

@@ -366,9 +366,8 @@ int fa_bwd(int dtype, int B, int S, int H, int D, const fa_tensor_t* q,
     float* delta = reinterpret_cast<float*>(ws);
     ws += align256((size_t)B * H * s_pad * 4);
     float* dq_acc = reinterpret_cast<float*>(ws);
-    FA_TRY(launch_bwd_delta(dtype, sh, o, d_o, lse, delta, lse2, s_pad, st));
-    const size_t acc_bytes = (size_t)B * H * s_pad * D * 4;
-    FA_TRY(record_cuda_error(cudaMemsetAsync(dq_acc, 0, acc_bytes, st)));
+    // Delta / LSE2 prologue; it also clears the dQ accumulator
+    FA_TRY(launch_bwd_delta(dtype, sh, o, d_o, lse, delta, lse2, s_pad, st, dq_acc));
     cudaEvent_t stop = timer_begin(FA_TIMER_BWD, st);
     const int rc = launch_attn_bwd_bf16(sh, S, &qr, &kr, v, d_o, lse2, delta,
                                         dq_acc, dk, dv, nullptr, nullptr, 0, scale,

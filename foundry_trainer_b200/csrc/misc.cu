@@ -217,6 +217,149 @@ rope_token_kernel(TView x0, TOut y0, TView x1, TOut y1,
   }
 }
 
+// bf16 -> bf16 rotation for the reference layout, eight tokens per block:
+// lane l of a half-warp owns elements 8l..8l+7 of a row (one 16-byte access;
+// the rotate-half partner of element 8l+u is element 8(l^2)+u), so a warp
+// instruction moves two rows. All of a thread's row loads are issued before
+// the block evaluates its tokens' (cos, sin) into shared memory.
+constexpr int kTokTokens = 8;
+constexpr int kTokThreads = 256;
+constexpr int kTokMaxRows = 12;  // rows per thread: 8 tokens x H <= 16 x 12 = 192 (H <= 24)
+__global__ void __launch_bounds__(kTokThreads)
+rope_tok8_bf16_kernel(TView x0, TOut y0, TView x1, TOut y1,
+                      const __grid_constant__ RopeArgs r, int S, int H, float alpha,
+                      int inverse) {
+  __shared__ float2 cs_s[kTokTokens][64];
+  const TView& x = blockIdx.y == 0 ? x0 : x1;
+  const TOut& y = blockIdx.y == 0 ? y0 : y1;
+  const int tiles = (S + kTokTokens - 1) / kTokTokens;
+  const int s0 = (int)(blockIdx.x % tiles) * kTokTokens, b = (int)(blockIdx.x / tiles);
+  const int hw = threadIdx.x >> 4;  // half-warp: one row per access
+  const int l = threadIdx.x & 15;
+  const int rows = kTokTokens * H;
+  const bool rotate = r.pos != nullptr;
+  uint4 v[kTokMaxRows];
+#pragma unroll
+  for (int k = 0; k < kTokMaxRows; ++k) {
+    const int row = hw + k * (kTokThreads / 16);
+    const int t = row / H, h = row - t * H, s = s0 + t;
+    if (row < rows && s < S)
+      v[k] = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(x.p) +
+                                              b * x.sb + (int64_t)s * x.ss + h * x.sh + 8 * l);
+  }
+  if (rotate) {
+    for (int i = threadIdx.x; i < kTokTokens * 64; i += kTokThreads) {
+      const int t = i >> 6, f = i & 63, s = s0 + t;
+      if (s < S) {
+        const int64_t ti = (int64_t)(s + r.pos_offset) * 64 + f;
+        const float2 c = r.table != nullptr ? r.table[ti] : rope_cs_direct(r, s, f);
+        cs_s[t][f] = c;
+        if (r.table_out != nullptr && b == 0 && blockIdx.y == 0) r.table_out[ti] = c;
+      }
+    }
+  }
+  __syncthreads();
+  // forward: first half y = x c - x' s, second half y = x c + x' s;
+  // inverse: the transposed rotation (signs swapped)
+  const bool first = (l & 3) < 2;
+  const float sgn = (first != (inverse != 0)) ? -1.f : 1.f;
+  const int f0 = (l >> 2) * 16 + (l & 1) * 8;  // frequencies f0..f0+7
+#pragma unroll
+  for (int k = 0; k < kTokMaxRows; ++k) {
+    const int row = hw + k * (kTokThreads / 16);
+    const int t = row / H, h = row - t * H, s = s0 + t;
+    const bool live = row < rows && s < S;  // uniform per half-warp
+    float e[8];
+    e[0] = __uint_as_float(v[k].x << 16); e[1] = __uint_as_float(v[k].x & 0xFFFF0000u);
+    e[2] = __uint_as_float(v[k].y << 16); e[3] = __uint_as_float(v[k].y & 0xFFFF0000u);
+    e[4] = __uint_as_float(v[k].z << 16); e[5] = __uint_as_float(v[k].z & 0xFFFF0000u);
+    e[6] = __uint_as_float(v[k].w << 16); e[7] = __uint_as_float(v[k].w & 0xFFFF0000u);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) e[u] *= alpha;
+    if (rotate) {
+      // partner values from lane l^2 (all 32 lanes take part in the shuffle)
+      float o[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) o[u] = __shfl_xor_sync(0xffffffffu, e[u], 2);
+      if (live) {
+        const int tt = t < kTokTokens ? t : 0;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const float2 c = cs_s[tt][f0 + u];
+          e[u] = __fadd_rn(__fmul_rn(e[u], c.x), __fmul_rn(sgn * o[u], c.y));
+        }
+      }
+    }
+    if (live)
+      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(y.p) + b * y.sb +
+                                (int64_t)s * y.ss + h * y.sh + 8 * l) =
+          make_uint4(pack_bf16(e[0], e[1]), pack_bf16(e[2], e[3]), pack_bf16(e[4], e[5]),
+                     pack_bf16(e[6], e[7]));
+  }
+}
+
+// delta / lse2 for bf16 O, dO with 16-byte accesses, eight tokens per block
+// (rows (token, head), a half-warp per row, every load issued first); the
+// block also clears its tokens' rows of the fp32 dQ accumulator
+// (B, H, s_pad, 128) when zero_acc is given.
+__global__ void __launch_bounds__(kTokThreads)
+delta_tok8_bf16_kernel(TView o, TView d_o, const float* lse, float* delta, float* lse2,
+                       float* zero_acc, int S, int H, int s_pad) {
+  __shared__ float sums[kTokMaxRows * (kTokThreads / 16)];
+  const int tiles = s_pad / kTokTokens;
+  const int s0 = (int)(blockIdx.x % tiles) * kTokTokens, b = (int)(blockIdx.x / tiles);
+  const int hw = threadIdx.x >> 4;
+  const int l = threadIdx.x & 15;
+  const int rows = kTokTokens * H;
+  uint4 a[kTokMaxRows], g[kTokMaxRows];
+#pragma unroll
+  for (int k = 0; k < kTokMaxRows; ++k) {
+    const int row = hw + k * (kTokThreads / 16);
+    const int t = row / H, h = row - t * H, s = s0 + t;
+    if (row < rows && s < S) {
+      a[k] = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(o.p) +
+                                              b * o.sb + (int64_t)s * o.ss + h * o.sh + 8 * l);
+      g[k] = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(d_o.p) +
+                                              b * d_o.sb + (int64_t)s * d_o.ss + h * d_o.sh + 8 * l);
+    } else {
+      a[k] = make_uint4(0, 0, 0, 0);
+      g[k] = make_uint4(0, 0, 0, 0);
+    }
+  }
+  if (zero_acc != nullptr) {
+    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i = threadIdx.x; i < rows * 32; i += kTokThreads) {
+      const int row = i >> 5, c = i & 31;
+      const int t = row / H, h = row - t * H;
+      reinterpret_cast<float4*>(zero_acc + (((int64_t)b * H + h) * s_pad + s0 + t) * 128)[c] = z;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kTokMaxRows; ++k) {
+    const uint32_t av[4] = {a[k].x, a[k].y, a[k].z, a[k].w};
+    const uint32_t gv[4] = {g[k].x, g[k].y, g[k].z, g[k].w};
+    float acc = 0.f;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      acc = fmaf(__uint_as_float(av[u] << 16), __uint_as_float(gv[u] << 16), acc);
+      acc = fmaf(__uint_as_float(av[u] & 0xFFFF0000u), __uint_as_float(gv[u] & 0xFFFF0000u), acc);
+    }
+#pragma unroll
+    for (int off = 8; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    const int row = hw + k * (kTokThreads / 16);
+    if (l == 0 && row < rows) sums[row] = acc;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < rows; i += kTokThreads) {
+    const int h = i / kTokTokens, t = i % kTokTokens;
+    const int64_t bh = (int64_t)b * H + h;
+    const int s = s0 + t;
+    delta[bh * s_pad + s] = sums[t * H + h];
+    if (lse2 != nullptr)
+      lse2[bh * s_pad + s] = (s < S) ? lse[bh * S + s] * 1.4426950408889634f : INFINITY;
+  }
+}
+
 // delta[b, h, s] = sum_d dO * O over s < s_pad (0 past S); lse2 likewise
 // (+inf past S). One block per 8 tokens of one b: each warp reduces rows
 // (token, head) four at a time (a lane holds 4 elements of each), the sums
@@ -354,10 +497,29 @@ static bool aligned16(const V& t, int dtype) {
          t.ss % 4 == 0 && t.sh % 4 == 0;
 }
 
+// 16-byte accesses of 8 bf16: rows aligned to 8 elements, strides multiples of 8
+template <typename V>
+static bool aligned16_8(const V& t) {
+  return (reinterpret_cast<uintptr_t>(t.p) % 16) == 0 && t.sb % 8 == 0 && t.ss % 8 == 0 &&
+         t.sh % 8 == 0;
+}
+
 int launch_bwd_delta(int dtype, const AttnShape& sh, const fa_tensor_t* o,
                      const fa_tensor_t* d_o, const float* lse, float* delta,
-                     float* lse2, int s_pad, cudaStream_t stream) {
+                     float* lse2, int s_pad, cudaStream_t stream, float* zero_acc) {
   const misc::TView ov = misc::tview(o), dv = misc::tview(d_o);
+  if (dtype == FA_DTYPE_BF16 && sh.D == 128 && sh.H <= 24 && s_pad % misc::kTokTokens == 0 &&
+      aligned16_8(ov) && aligned16_8(dv)) {
+    const dim3 grid((unsigned)((int64_t)sh.B * (s_pad / misc::kTokTokens)));
+    misc::delta_tok8_bf16_kernel<<<grid, misc::kTokThreads, 0, stream>>>(
+        ov, dv, lse, delta, lse2, zero_acc, sh.S, sh.H, s_pad);
+    return launch_status();
+  }
+  if (zero_acc != nullptr) {
+    const int rc = record_cuda_error(cudaMemsetAsync(
+        zero_acc, 0, (size_t)sh.B * sh.H * s_pad * sh.D * sizeof(float), stream));
+    if (rc != FA_OK) return rc;
+  }
   if (sh.D == 128 && sh.H <= misc::kDeltaMaxHeads && s_pad % misc::kDeltaTokens == 0 &&
       aligned16(ov, dtype) && aligned16(dv, dtype)) {
     const dim3 grid((unsigned)((int64_t)sh.B * (s_pad / misc::kDeltaTokens)));
@@ -406,6 +568,14 @@ static int launch_rope_generic(int dtype_in, int dtype_out, const AttnShape& sh,
     rr.table = r.table_out;
     rr.table_out = nullptr;
     return launch_rope_generic(dtype_in, dtype_out, sh, x, y, rr, alpha, inverse, stream, xb, yb);
+  }
+  if (token_path && dtype_in == FA_DTYPE_BF16 && dtype_out == FA_DTYPE_BF16 &&
+      sh.H <= 24 && aligned16_8(x) && aligned16_8(y) && aligned16_8(x2) && aligned16_8(y2)) {
+    const int tiles = (sh.S + misc::kTokTokens - 1) / misc::kTokTokens;
+    const dim3 grid((unsigned)((int64_t)sh.B * tiles), npairs);
+    misc::rope_tok8_bf16_kernel<<<grid, misc::kTokThreads, 0, stream>>>(x, y, x2, y2, r, sh.S,
+                                                                       sh.H, alpha, inverse);
+    return launch_status();
   }
   if (token_path) {
     const dim3 grid((unsigned)((int64_t)sh.B * sh.S), npairs);
