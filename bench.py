@@ -263,9 +263,12 @@ def main():
             dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
             outs = {"o": o, "dq": dq, "dk": dk, "dv": dv}
 
+            saved = {}
+
             def step():
-                ops.attn_fwd(q, k, v, rope=rope, out=o, lse=lse)
-                ops.attn_bwd(q, k, v, o, d_o, lse, rope=rope, dq=dq, dk=dk, dv=dv)
+                # the backward reuses the forward's rotated q, k (fa_bwd_saved)
+                ops.attn_fwd(q, k, v, rope=rope, out=o, lse=lse, saved=saved)
+                ops.attn_bwd(q, k, v, o, d_o, lse, rope=rope, dq=dq, dk=dk, dv=dv, saved=saved)
             return step, outs
     step, outs = make_step(q, k, v, d_o)
     flush_buf = torch.empty(256 * 1024 * 1024 // 4, device=dev, dtype=torch.float32)
@@ -454,7 +457,7 @@ def main():
                "ms_per_step": te.item() / K,
                "path": ("ring.ring_fwd + ring.ring_bwd (C ABI fa_fwd_partial/fa_bwd_partial "
                         "round an NCCL ring)" if ring_mode else
-                        "ops.attn_fwd + ops.attn_bwd (C ABI fa_fwd/fa_bwd)") +
+                        "ops.attn_fwd + ops.attn_bwd (C ABI fa_fwd/fa_bwd_saved)") +
                        " per rank; every step copies its pinned host q,k,v,dO in and o,dq,dk,dv "
                        "out; copies of the neighbouring steps overlap the compute on separate "
                        "streams (the timed region covers all K steps' copies and compute)"}
@@ -480,7 +483,7 @@ def main():
                     f"{n_loc} rows per rank, non-causal, axial RoPE")
         parallelism = f"sequence ring x{world} (NCCL send/recv of K,V and fp32 dK,dV)"
     else:
-        launches_per_step = 8  # rope q,k + fwd; rope q,k + delta + bwd + dQ cast
+        launches_per_step = 5  # rope q,k (+ table) + fwd; delta (+ dQ clear) + bwd + dQ finish
         workload = (f"{cfg.name}: B={cfg.B} H={cfg.H} S={cfg.S} "
                     f"({cfg.txt} text + {cfg.grid}x{cfg.grid} image) D={cfg.D} "
                     f"per rank, non-causal, axial RoPE inside the op")

@@ -25,6 +25,12 @@ from . import ops
 from ._lib import FaError
 
 
+def _tensor_key(q: torch.Tensor, k: torch.Tensor):
+    """Identity of the (q, k) a forward rotated: storage, layout and version."""
+    return (q.data_ptr(), tuple(q.stride()), q._version, k.data_ptr(), tuple(k.stride()),
+            k._version)
+
+
 class AttnBwd:
     """The joint-attention op, CustomOp3-shaped (lib.rs:151-264)."""
 
@@ -34,6 +40,8 @@ class AttnBwd:
         self.rope = rope
         self.deterministic = deterministic
         self._saved_lse: Optional[torch.Tensor] = None
+        # with rope: the forward's rotated q, k and (cos, sin) table, reused by bwd
+        self._saved_fwd: dict = {}
 
     def name(self) -> str:
         return "foundry-attn-bwd"  # lib.rs:154-156
@@ -44,7 +52,9 @@ class AttnBwd:
 
     def cuda_fwd(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
         """Forward on device storage (lib.rs:189-214); keeps the LSE for bwd."""
-        out, lse = ops.attn_fwd(q, k, v, scale=self.scale, rope=self.rope)
+        out, lse = ops.attn_fwd(q, k, v, scale=self.scale, rope=self.rope,
+                                saved=self._saved_fwd)
+        self._saved_fwd["key"] = _tensor_key(q, k)
         self._saved_lse = lse
         return out
 
@@ -56,8 +66,10 @@ class AttnBwd:
             # Called without a preceding cuda_fwd on this instance: rebuild the
             # statistics with one forward pass.
             _, lse = ops.attn_fwd(q, k, v, scale=self.scale, rope=self.rope)
+        # the forward's rotated q, k are reused only for the very tensors it saw
+        saved = self._saved_fwd if self._saved_fwd.get("key") == _tensor_key(q, k) else None
         return ops.attn_bwd(q, k, v, res, grad_res.contiguous(), lse, scale=self.scale,
-                            rope=self.rope, deterministic=self.deterministic)
+                            rope=self.rope, deterministic=self.deterministic, saved=saved)
 
     def fwd(self, q, k, v):
         if q.is_cuda:
@@ -71,6 +83,7 @@ class _Op3(torch.autograd.Function):
         out = op.fwd(q, k, v)
         ctx.op = op
         ctx.lse = op._saved_lse
+        ctx.saved_fwd = dict(op._saved_fwd)
         ctx.save_for_backward(q, k, v, out)
         return out
 
@@ -79,6 +92,7 @@ class _Op3(torch.autograd.Function):
         q, k, v, out = ctx.saved_tensors
         op: AttnBwd = ctx.op
         op._saved_lse = ctx.lse
+        op._saved_fwd = ctx.saved_fwd
         dq, dk, dv = op.bwd(q, k, v, out, grad_out)
         return dq, dk, dv, None
 

@@ -261,11 +261,12 @@ int fa_device_status(void) {
   return first;
 }
 
+// forward workspace (RoPE inside the op): [q_rot | k_rot | (cos, sin) table]
 size_t fa_fwd_workspace_bytes(int dtype, int B, int S, int H, int D,
                               const fa_rope_t* rope) {
   if (rope == nullptr) return 0;
   const size_t es = dtype == FA_DTYPE_BF16 ? 2 : 4;
-  return 2 * align256((size_t)B * S * H * D * es);
+  return 2 * align256((size_t)B * S * H * D * es) + rope_table_bytes(S, rope);
 }
 
 int fa_fwd(int dtype, int B, int S, int H, int D, const fa_tensor_t* q,
@@ -293,7 +294,9 @@ int fa_fwd(int dtype, int B, int S, int H, int D, const fa_tensor_t* q,
     const size_t tb = align256((size_t)B * S * H * D * es);
     qr = contiguous_view(ws, S, H, D);
     kr = contiguous_view(ws + tb, S, H, D);
-    FA_TRY(launch_rope_pair(dtype, sh, q, &qr, k, &kr, rope, 0, 0, st, nullptr));
+    // the rotation pass also leaves the (cos, sin) table for fa_bwd_saved
+    float2* table = reinterpret_cast<float2*>(ws + 2 * tb);
+    FA_TRY(launch_rope_pair(dtype, sh, q, &qr, k, &kr, rope, 0, 0, st, nullptr, table));
   }
   cudaEvent_t stop = timer_begin(FA_TIMER_FWD, st);
   const int rc = bf ? launch_attn_fwd_bf16(sh, S, &qr, &kr, v, o, lse, scale, st)
@@ -398,6 +401,56 @@ int fa_bwd(int dtype, int B, int S, int H, int D, const fa_tensor_t* q,
   FA_TRY(rc);
   if (rope) FA_TRY(launch_rope_pair(dtype, sh, &dqr, dq, &dkr, dk, rope, 1, 0, st, table));
   return FA_OK;
+}
+
+size_t fa_bwd_saved_workspace_bytes(int dtype, int B, int S, int H, int D) {
+  if (dtype != FA_DTYPE_BF16) return 0;
+  const size_t s_pad = (size_t)((S + 127) / 128) * 128;
+  return 2 * align256((size_t)B * H * s_pad * 4) + align256((size_t)B * H * s_pad * D * 4);
+}
+
+int fa_bwd_saved(int dtype, int B, int S, int H, int D, const void* fwd_workspace,
+                 size_t fwd_workspace_bytes, const fa_tensor_t* v, const fa_tensor_t* o,
+                 const fa_tensor_t* d_o, const float* lse, const fa_tensor_t* dq,
+                 const fa_tensor_t* dk, const fa_tensor_t* dv, float scale,
+                 const fa_rope_t* rope, void* workspace, size_t workspace_bytes,
+                 void* stream) {
+  FA_TRY(check_shape(dtype, B, S, H, D));
+  if (dtype != FA_DTYPE_BF16) return FA_ERR_UNSUPPORTED;
+  if (rope == nullptr) return FA_ERR_INVALID_ARG;  // without RoPE call fa_bwd
+  FA_TRY(check_rope(rope, D));
+  if (!(scale > 0.f) || !std::isfinite(scale)) return FA_ERR_INVALID_ARG;
+  FA_TRY(check_tensor(v, 2, true));
+  FA_TRY(check_tensor(d_o, 2, true));
+  for (const fa_tensor_t* t : {o, dq, dk, dv}) FA_TRY(check_tensor(t, 2, true));
+  if (lse == nullptr || fwd_workspace == nullptr) return FA_ERR_INVALID_ARG;
+  if (fwd_workspace_bytes < fa_fwd_workspace_bytes(dtype, B, S, H, D, rope))
+    return FA_ERR_WORKSPACE;
+  if (workspace == nullptr || workspace_bytes < fa_bwd_saved_workspace_bytes(dtype, B, S, H, D))
+    return FA_ERR_WORKSPACE;
+  FA_TRY(check_sm100());
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const AttnShape sh{B, S, H, D};
+  // the forward's rotated q, k and (cos, sin) table
+  uint8_t* fws = reinterpret_cast<uint8_t*>(const_cast<void*>(fwd_workspace));
+  const size_t tb = align256((size_t)B * S * H * D * 2);
+  const fa_tensor_t qr = contiguous_view(fws, S, H, D);
+  const fa_tensor_t kr = contiguous_view(fws + tb, S, H, D);
+  const float2* table = reinterpret_cast<const float2*>(fws + 2 * tb);
+  const int s_pad = ((S + 127) / 128) * 128;
+  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+  float* lse2 = reinterpret_cast<float*>(ws);
+  ws += align256((size_t)B * H * s_pad * 4);
+  float* delta = reinterpret_cast<float*>(ws);
+  ws += align256((size_t)B * H * s_pad * 4);
+  float* dq_acc = reinterpret_cast<float*>(ws);
+  FA_TRY(launch_bwd_delta(dtype, sh, o, d_o, lse, delta, lse2, s_pad, st, dq_acc));
+  cudaEvent_t stop = timer_begin(FA_TIMER_BWD, st);
+  const int rc = launch_attn_bwd_bf16(sh, S, &qr, &kr, v, d_o, lse2, delta, dq_acc, dk, dv,
+                                      nullptr, nullptr, 0, scale, rope, table, st);
+  timer_end(stop, st);
+  FA_TRY(rc);
+  return launch_cast_f32(dtype, sh, dq_acc, dq, scale, rope, 0, st, table, s_pad);
 }
 
 int fa_rope_apply(int dtype, int B, int S, int H, int D, const fa_tensor_t* x,

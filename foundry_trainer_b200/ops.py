@@ -80,8 +80,12 @@ def default_scale(d: int) -> float:
 
 def attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: Optional[float] = None,
              rope: Optional[Rope] = None, out: Optional[torch.Tensor] = None,
-             lse: Optional[torch.Tensor] = None, stream=None):
-    """O and fp32 LSE (B, H, S) of softmax(Q K^T * scale) V."""
+             lse: Optional[torch.Tensor] = None, stream=None, saved: Optional[dict] = None):
+    """O and fp32 LSE (B, H, S) of softmax(Q K^T * scale) V.
+
+    With `rope` and a `saved` dict, the forward's workspace (rotated q, k and
+    their (cos, sin) table) is kept in it for attn_bwd(..., saved=...), which
+    then skips the second rotation."""
     q4, k4, v4 = as_bshd(q), as_bshd(k), as_bshd(v)
     B, S, H, D = q4.shape
     if k4.shape != q4.shape or v4.shape != q4.shape:
@@ -98,6 +102,10 @@ def attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: Option
     rc_rope = rope.c_struct() if rope is not None else None
     ws_bytes = lib.fa_fwd_workspace_bytes(dt, B, S, H, D, _ref(rc_rope))
     ws = torch.empty(ws_bytes, device=q.device, dtype=torch.uint8) if ws_bytes else None
+    if saved is not None:
+        saved.clear()
+        if ws is not None:
+            saved.update(ws=ws, shape=(B, S, H, D), dtype=q.dtype)
     dq_, dk_, dv_, do_ = desc(q4), desc(k4), desc(v4), desc(as_bshd(out))
     check(lib.fa_fwd(dt, B, S, H, D, C.byref(dq_), C.byref(dk_), C.byref(dv_), C.byref(do_),
                      lse.data_ptr(), scale, _ref(rc_rope), ws.data_ptr() if ws is not None else None,
@@ -106,8 +114,12 @@ def attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: Option
 
 
 def attn_bwd(q, k, v, o, d_o, lse, *, scale: Optional[float] = None, rope: Optional[Rope] = None,
-             deterministic: bool = False, dq=None, dk=None, dv=None, stream=None):
-    """dQ, dK, dV of the op (w.r.t. pre-rotation q/k when rope is given)."""
+             deterministic: bool = False, dq=None, dk=None, dv=None, stream=None,
+             saved: Optional[dict] = None):
+    """dQ, dK, dV of the op (w.r.t. pre-rotation q/k when rope is given).
+
+    `saved`: the dict a matching attn_fwd(..., saved=...) filled; the bf16
+    path then reuses the forward's rotated q, k (fa_bwd_saved)."""
     q4 = as_bshd(q)
     B, S, H, D = q4.shape
     dt = _dtype_code(q)
@@ -117,6 +129,17 @@ def attn_bwd(q, k, v, o, d_o, lse, *, scale: Optional[float] = None, rope: Optio
     scale = default_scale(D) if scale is None else float(scale)
     lib = _lib.load()
     rc_rope = rope.c_struct() if rope is not None else None
+    if (saved and rope is not None and dt == FA_DTYPE_BF16 and not deterministic
+            and saved.get("shape") == (B, S, H, D) and saved.get("dtype") == q.dtype):
+        fws = saved["ws"]
+        ws_bytes = lib.fa_bwd_saved_workspace_bytes(dt, B, S, H, D)
+        ws = torch.empty(ws_bytes, device=q.device, dtype=torch.uint8)
+        ds = [desc(x) for x in (v, o, d_o, dq, dk, dv)]
+        check(lib.fa_bwd_saved(dt, B, S, H, D, fws.data_ptr(), fws.numel(),
+                               *[C.byref(x) for x in ds[:3]], lse.data_ptr(),
+                               *[C.byref(x) for x in ds[3:]], scale, C.byref(rc_rope),
+                               ws.data_ptr(), ws_bytes, _stream_ptr(stream)), "fa_bwd_saved")
+        return dq, dk, dv
     ws_bytes = lib.fa_bwd_workspace_bytes(dt, B, S, H, D, _ref(rc_rope), int(deterministic))
     ws = torch.empty(max(ws_bytes, 1), device=q.device, dtype=torch.uint8)
     ds = [desc(x) for x in (q, k, v, o, d_o, dq, dk, dv)]

@@ -82,8 +82,9 @@ typedef struct {
  * recomputes it instead (lib.rs:232-238).
  * If `rope` is non-NULL, q and k are pre-rotation and the rotation is applied
  * inside the op (the reference applies it before the op, lib.rs:326-358).
- * `workspace` (may be NULL when fa_fwd_workspace_bytes() returns 0) holds the
- * rotated keys and must stay untouched until the matching fa_bwd returns.
+ * `workspace` (may be NULL when fa_fwd_workspace_bytes() returns 0) receives
+ * the rotated q and k and their (cos, sin) table, which fa_bwd_saved can
+ * reuse.
  */
 int fa_fwd(int dtype, int B, int S, int H, int D,
            const fa_tensor_t* q, const fa_tensor_t* k, const fa_tensor_t* v,
@@ -112,6 +113,24 @@ int fa_bwd(int dtype, int B, int S, int H, int D,
 
 size_t fa_bwd_workspace_bytes(int dtype, int B, int S, int H, int D,
                               const fa_rope_t* rope, int deterministic);
+
+/*
+ * Backward that reuses the forward's rotation (bf16, RoPE inside the op).
+ * fa_fwd with `rope` leaves in its workspace the rotated q, k and the
+ * (cos, sin) table; passing that workspace here (`fwd_workspace`, untouched
+ * since the forward) skips the second rotation of q and k that fa_bwd does.
+ * The reference's backward likewise works on the rotated q, k saved as the
+ * op's inputs (lib.rs:216-263). Results equal fa_bwd's for the same inputs.
+ * `workspace` must hold fa_bwd_saved_workspace_bytes().
+ */
+int fa_bwd_saved(int dtype, int B, int S, int H, int D,
+                 const void* fwd_workspace, size_t fwd_workspace_bytes,
+                 const fa_tensor_t* v, const fa_tensor_t* o, const fa_tensor_t* d_o,
+                 const float* lse, const fa_tensor_t* dq, const fa_tensor_t* dk,
+                 const fa_tensor_t* dv, float scale, const fa_rope_t* rope,
+                 void* workspace, size_t workspace_bytes, void* stream);
+
+size_t fa_bwd_saved_workspace_bytes(int dtype, int B, int S, int H, int D);
 
 /*
  * Standalone rotation, the reference's apply_rope (lib.rs:122-129) for

@@ -128,3 +128,50 @@ def test_c2_full_size_properties():
     # => sum_s dK[s] = scale * sum_q (sum_k dS[q,k]) Q[q] = 0
     sk = dk.float().sum(dim=1).abs().max().item()
     assert sk < 2e-2 * dk.float().abs().max().item() * 64
+
+
+def test_bf16_bwd_saved_reuses_forward_rotation():
+    """fa_bwd_saved (the forward's rotated q, k and table) gives fa_bwd's result."""
+    from foundry_trainer_b200 import configs, ops
+    g = torch.Generator().manual_seed(21)
+    txt, grid = 104, 24  # 104 text + 24x24 image tokens
+    B, S, H = 1, txt + grid * grid, 3
+    q, k, v = ((torch.randn(B, S, H, 128, generator=g) * 0.5).to(torch.bfloat16).cuda()
+               for _ in range(3))
+    d_o = torch.randn(B, S, H, 128, generator=g).to(torch.bfloat16).cuda()
+    pos = configs.positions(txt, grid)
+    rope = ops.Rope(pos.cuda())
+    saved = {}
+    o, lse = ops.attn_fwd(q, k, v, rope=rope, saved=saved)
+    assert saved and saved["ws"].numel() > 0
+    got = ops.attn_bwd(q, k, v, o, d_o, lse, rope=rope, saved=saved)
+    ref = ops.attn_bwd(q, k, v, o, d_o, lse, rope=rope)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    for name, a, b in zip(("dq", "dk", "dv"), got, ref):
+        # same kernels on the same data; dQ's fp32 reductions may land in another order
+        err = orc.max_rel(np32(a), np32(b))
+        assert err <= 1e-2, (name, err)
+    ro, rlse, rdq, rdk, rdv = orc.attn_fwd_bwd_bshd(np32(q), np32(k), np32(v), np32(d_o), "bf16",
+                                                    rope_pos=pos.numpy())
+    assert_close({"o": np32(o), "dq": np32(got[0]), "dk": np32(got[1]), "dv": np32(got[2])},
+                 {"o": ro, "dq": rdq, "dk": rdk, "dv": rdv}, TOL, "bwd_saved")
+
+
+def test_bf16_op_mirror_with_rope_under_autograd():
+    """AttnBwd with RoPE through apply_op3: the backward reuses the forward's rotation."""
+    from foundry_trainer_b200 import attn, configs, ops
+    g = torch.Generator().manual_seed(23)
+    pos = configs.positions(64, 16)
+    B, S, H = 1, pos.shape[0], 2
+    q, k, v = ((torch.randn(B, S, H, 128, generator=g) * 0.5).to(torch.bfloat16).cuda()
+               .requires_grad_(True) for _ in range(3))
+    d_o = torch.randn(B, S, H, 128, generator=g).to(torch.bfloat16).cuda()
+    op = attn.AttnBwd(rope=ops.Rope(pos.cuda()))
+    out = attn.apply_op3(q, k, v, op)
+    out.backward(d_o)
+    torch.cuda.synchronize()
+    ro, _, rdq, rdk, rdv = orc.attn_fwd_bwd_bshd(np32(q), np32(k), np32(v), np32(d_o), "bf16",
+                                                 rope_pos=pos.numpy())
+    assert_close({"o": np32(out), "dq": np32(q.grad), "dk": np32(k.grad), "dv": np32(v.grad)},
+                 {"o": ro, "dq": rdq, "dk": rdk, "dv": rdv}, TOL, "op3 rope")
