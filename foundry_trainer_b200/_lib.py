@@ -66,6 +66,8 @@ SIGNATURES = {
                                 C.c_void_p]),
     "fa_fwd_partial": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _T, _T, _T,
                                  _T, _F, C.c_float, C.c_void_p]),
+    "fa_fwd_fold": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _T, _T, _T,
+                              _F, _F, C.c_int, C.c_int, _T, _F, C.c_float, C.c_void_p]),
     "fa_lse_merge": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _F, _F, _T, _F,
                                C.c_int, C.c_void_p]),
     "fa_bwd_prepare": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _T, _T, _F, _F, _F,

@@ -45,10 +45,13 @@ void record_error_text(const char* msg);
 int ensure_smem_attr(const void* fn, int bytes, int kernel_id);
 
 // bf16 sm_100a kernels
+// merge: 0 plain; 1 (o_acc, lse_acc) <- block; 2 fold block into them;
+// 3 fold, then write o (bf16) and lse (see the kernel's Params)
 int launch_attn_fwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
                          const fa_tensor_t* k, const fa_tensor_t* v,
                          const fa_tensor_t* o, float* lse, float scale,
-                         cudaStream_t stream);
+                         cudaStream_t stream, int merge = 0, float* o_acc = nullptr,
+                         float* lse_acc = nullptr);
 
 int launch_attn_bwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
                          const fa_tensor_t* k, const fa_tensor_t* v,

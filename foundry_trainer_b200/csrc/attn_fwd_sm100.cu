@@ -82,6 +82,12 @@ struct Params {
   int S, H, kv_len, nkv;
   float scale_log2;  // scale * log2(e)
   float* lse;        // (B, H, S)
+  // Sequence-block folding (ring attention): 0 plain (O through tm_o, LSE);
+  // 1 first block: (o_acc, lse_acc) <- this block; 2 fold this block into
+  // (o_acc, lse_acc); 3 fold, then write the final O (tm_o) and LSE (lse).
+  int merge;
+  float* o_acc;      // fp32 contiguous (B, S, H, D), normalised rows
+  float* lse_acc;    // (B, H, S), natural log
 };
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -311,7 +317,22 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
     stop = __any_sync(0xffffffffu, stop);
     if (!named_bar_any(bar_id, 128, stop)) {
       tc_fence_after();
-      const float inv_l = 1.f / l_run;
+      const int row0 = (pair * kTiles + t) * kRows;
+      const int row = row0 + row_in_tile;
+      const bool live = row < p.S;
+      const float lse_blk = (m_run + __log2f(l_run)) * 0.69314718055994531f;
+      // this row's O = wb * (block O / l) + wa * o_acc, LSE = lse_out
+      float wb = 1.f / l_run, wa = 0.f, lse_out = lse_blk;
+      const int64_t acc_row = (((int64_t)b * p.S + row) * p.H + h) * 128;
+      if (p.merge >= 2 && live) {
+        const float la = p.lse_acc[((int64_t)b * p.H + h) * p.S + row];
+        const float mx = fmaxf(la, lse_blk);
+        const float ea = expf(la - mx), eb = expf(lse_blk - mx);
+        const float inv = 1.f / (ea + eb);
+        wa = ea * inv;
+        wb = eb * inv / l_run;
+        lse_out = mx + logf(ea + eb);
+      }
       uint8_t* stage = smem + kOffQ + t * kTileBytes;
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
@@ -319,33 +340,54 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
         tmem_ld32(t_o + half * 64, orow);
         tmem_ld32(t_o + half * 64 + 32, orow + 32);
         tmem_wait_ld();
+        float* ov = reinterpret_cast<float*>(orow);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint4 v;
-          v.x = pack_bf16(__uint_as_float(orow[c * 8 + 0]) * inv_l,
-                          __uint_as_float(orow[c * 8 + 1]) * inv_l);
-          v.y = pack_bf16(__uint_as_float(orow[c * 8 + 2]) * inv_l,
-                          __uint_as_float(orow[c * 8 + 3]) * inv_l);
-          v.z = pack_bf16(__uint_as_float(orow[c * 8 + 4]) * inv_l,
-                          __uint_as_float(orow[c * 8 + 5]) * inv_l);
-          v.w = pack_bf16(__uint_as_float(orow[c * 8 + 6]) * inv_l,
-                          __uint_as_float(orow[c * 8 + 7]) * inv_l);
-          *reinterpret_cast<uint4*>(stage + half * kBlkBytes + sw128_offset(row_in_tile, c)) = v;
+        for (int c = 0; c < 64; ++c) ov[c] *= wb;
+        if (p.merge >= 2 && live) {
+          const float4* a4 = reinterpret_cast<const float4*>(p.o_acc + acc_row + half * 64);
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            const float4 a = a4[c];
+            ov[4 * c + 0] = fmaf(a.x, wa, ov[4 * c + 0]);
+            ov[4 * c + 1] = fmaf(a.y, wa, ov[4 * c + 1]);
+            ov[4 * c + 2] = fmaf(a.z, wa, ov[4 * c + 2]);
+            ov[4 * c + 3] = fmaf(a.w, wa, ov[4 * c + 3]);
+          }
+        }
+        if (p.merge == 1 || p.merge == 2) {
+          if (live) {
+            float4* d4 = reinterpret_cast<float4*>(p.o_acc + acc_row + half * 64);
+#pragma unroll
+            for (int c = 0; c < 16; ++c)
+              d4[c] = make_float4(ov[4 * c], ov[4 * c + 1], ov[4 * c + 2], ov[4 * c + 3]);
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            uint4 v;
+            v.x = pack_bf16(ov[c * 8 + 0], ov[c * 8 + 1]);
+            v.y = pack_bf16(ov[c * 8 + 2], ov[c * 8 + 3]);
+            v.z = pack_bf16(ov[c * 8 + 4], ov[c * 8 + 5]);
+            v.w = pack_bf16(ov[c * 8 + 6], ov[c * 8 + 7]);
+            *reinterpret_cast<uint4*>(stage + half * kBlkBytes + sw128_offset(row_in_tile, c)) = v;
+          }
         }
       }
-      fence_proxy_async_smem();
-      named_bar_sync(bar_id, 128);
-      const int row0 = (pair * kTiles + t) * kRows;
-      if (warp == 4 * t && lane == 0) {
-        tma_store_4d(&tm_o, stage, 0, row0, h, b);
-        tma_store_4d(&tm_o, stage + kBlkBytes, 64, row0, h, b);
-        bulk_commit_group();
-        bulk_wait_group0();
+      if (p.merge == 0 || p.merge == 3) {
+        fence_proxy_async_smem();
+        named_bar_sync(bar_id, 128);
+        if (warp == 4 * t && lane == 0) {
+          tma_store_4d(&tm_o, stage, 0, row0, h, b);
+          tma_store_4d(&tm_o, stage + kBlkBytes, 64, row0, h, b);
+          bulk_commit_group();
+          bulk_wait_group0();
+        }
       }
-      const int row = row0 + row_in_tile;
-      if (row < p.S)
-        p.lse[((int64_t)b * p.H + h) * p.S + row] =
-            (m_run + __log2f(l_run)) * 0.69314718055994531f;
+      if (live) {
+        const int64_t li = ((int64_t)b * p.H + h) * p.S + row;
+        if (p.merge == 1 || p.merge == 2) p.lse_acc[li] = lse_out;
+        else p.lse[li] = lse_out;
+      }
     } else {
       *abort_flag = 1;
     }
@@ -365,12 +407,14 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
 int launch_attn_fwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
                          const fa_tensor_t* k, const fa_tensor_t* v,
                          const fa_tensor_t* o, float* lse, float scale,
-                         cudaStream_t stream) {
+                         cudaStream_t stream, int merge, float* o_acc,
+                         float* lse_acc) {
   CUtensorMap tq, tk, tv, to;
   int rc = make_tmap_bshd(&tq, q, sh.B, sh.S, sh.H, sh.D, 128);
   if (!rc) rc = make_tmap_bshd(&tk, k, sh.B, kv_len, sh.H, sh.D, 128);
   if (!rc) rc = make_tmap_bshd(&tv, v, sh.B, kv_len, sh.H, sh.D, 128);
-  if (!rc) rc = make_tmap_bshd(&to, o, sh.B, sh.S, sh.H, sh.D, 128);
+  // modes 1 and 2 write no bf16 O: the map is encoded over q and never used
+  if (!rc) rc = make_tmap_bshd(&to, (merge == 1 || merge == 2) ? q : o, sh.B, sh.S, sh.H, sh.D, 128);
   if (rc) return rc;
   fwd::Params p;
   p.S = sh.S;
@@ -379,6 +423,9 @@ int launch_attn_fwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
   p.nkv = (kv_len + fwd::kKeys - 1) / fwd::kKeys;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.lse = lse;
+  p.merge = merge;
+  p.o_acc = o_acc;
+  p.lse_acc = lse_acc;
   rc = ensure_smem_attr((const void*)fwd::attn_fwd_kernel, fwd::kSmemBytes,
                         kKernelFwdBf16);
   if (rc) return rc;

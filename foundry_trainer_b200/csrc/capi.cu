@@ -489,6 +489,31 @@ int fa_fwd_partial(int dtype, int B, int S, int kv_len, int H, int D,
   return rc;
 }
 
+int fa_fwd_fold(int dtype, int B, int S, int kv_len, int H, int D,
+                const fa_tensor_t* q, const fa_tensor_t* k, const fa_tensor_t* v,
+                float* o_acc, float* lse_acc, int step, int last,
+                const fa_tensor_t* o, float* lse, float scale, void* stream) {
+  FA_TRY(check_shape(dtype, B, S, H, D));
+  if (dtype != FA_DTYPE_BF16) return FA_ERR_UNSUPPORTED;  // fp32: fa_fwd_partial + fa_lse_merge
+  if (kv_len <= 0 || step < 0) return FA_ERR_INVALID_ARG;
+  if (!(scale > 0.f) || !std::isfinite(scale)) return FA_ERR_INVALID_ARG;
+  for (const fa_tensor_t* t : {q, k, v}) FA_TRY(check_tensor(t, 2, true));
+  const int mode = step == 0 ? (last ? 0 : 1) : (last ? 3 : 2);
+  if (mode != 0 && (o_acc == nullptr || lse_acc == nullptr)) return FA_ERR_INVALID_ARG;
+  if (mode != 0 && reinterpret_cast<uintptr_t>(o_acc) % 16 != 0) return FA_ERR_ALIGNMENT;
+  if (last) {
+    FA_TRY(check_tensor(o, 2, true));
+    if (lse == nullptr) return FA_ERR_INVALID_ARG;
+  }
+  FA_TRY(check_sm100());
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  cudaEvent_t stop = timer_begin(FA_TIMER_FWD, st);
+  const int rc = launch_attn_fwd_bf16(AttnShape{B, S, H, D}, kv_len, q, k, v, last ? o : nullptr,
+                                      lse, scale, st, mode, o_acc, lse_acc);
+  timer_end(stop, st);
+  return rc;
+}
+
 int fa_lse_merge(int dtype, int B, int S, int H, int D, float* o_acc,
                  float* lse_acc, const fa_tensor_t* o_blk,
                  const float* lse_blk, int first, void* stream) {

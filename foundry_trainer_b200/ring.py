@@ -8,10 +8,10 @@ group and computes the same result with one exchange pattern, a ring:
 
   forward   each rank keeps its query rows Q_r and passes the K/V shards
             round the ring (rank r sends to r+1, receives from r-1). At step
-            t it attends its rows to shard (r - t) mod W with
-            `fa_fwd_partial` and folds the block into fp32 (O, LSE)
-            accumulators with `fa_lse_merge`; the next shard's transfer runs
-            on NCCL's stream while the block computes.
+            t it attends its rows to shard (r - t) mod W with `fa_fwd_fold`,
+            whose epilogue folds the block into fp32 (O, LSE) accumulators
+            (and on the last step writes the final bf16 O and LSE); the next
+            shard's transfer runs on NCCL's stream while the block computes.
   backward  K/V shards travel the same way; each shard's fp32 dK/dV
             accumulator travels one step behind it. At step t a rank writes
             the block's dK/dV to a local buffer (`fa_bwd_partial`, store
@@ -84,6 +84,16 @@ class RingKernels:
                                          lse_blk.data_ptr(), scale, ops._stream_ptr(None)),
               "fa_fwd_partial")
 
+    def fwd_fold(self, q, k, v, scale, o_acc, lse_acc, step: int, last: bool, o, lse) -> None:
+        B, S, H, D = q.shape
+        kv_len = k.shape[1]
+        dq_, dk_, dv_, do_ = ops.desc(q), ops.desc(k), ops.desc(v), ops.desc(o)
+        check(_lib.load().fa_fwd_fold(ops._dtype_code(q), B, S, kv_len, H, D, C.byref(dq_),
+                                      C.byref(dk_), C.byref(dv_), o_acc.data_ptr(),
+                                      lse_acc.data_ptr(), step, int(last), C.byref(do_),
+                                      lse.data_ptr(), scale, ops._stream_ptr(None)),
+              "fa_fwd_fold")
+
     def lse_merge(self, o_acc, lse_acc, o_blk, lse_blk, first: bool) -> None:
         B, S, H, D = o_blk.shape
         d = ops.desc(o_blk)
@@ -140,9 +150,9 @@ def ring_fwd(q, k, v, pos, scale, comm: RingComm, kern):
         q_r, k_r = q, k.contiguous()
     v_c = v.contiguous()
     o_acc = torch.empty((B, S, H, D), device=dev, dtype=torch.float32)
+    lse_acc = torch.empty((B, H, S), device=dev, dtype=torch.float32)
+    o = torch.empty((B, S, H, D), device=dev, dtype=q.dtype)
     lse = torch.empty((B, H, S), device=dev, dtype=torch.float32)
-    o_blk = torch.empty((B, S, H, D), device=dev, dtype=q.dtype)
-    lse_blk = torch.empty((B, H, S), device=dev, dtype=torch.float32)
     bufs = [[torch.empty_like(k_r), torch.empty_like(v_c)] for _ in range(2)] if comm.world > 1 else []
     cur = [k_r, v_c]
     for t in range(comm.world):
@@ -150,12 +160,12 @@ def ring_fwd(q, k, v, pos, scale, comm: RingComm, kern):
         if t < comm.world - 1:
             nxt = bufs[t % 2]
             works = comm.exchange(cur, nxt)
-        kern.fwd_partial(q_r, cur[0], cur[1], scale, o_blk, lse_blk)
-        kern.lse_merge(o_acc, lse, o_blk, lse_blk, t == 0)
+        # the block folds into (o_acc, lse_acc) inside the kernel; the last
+        # block writes the final o and lse
+        kern.fwd_fold(q_r, cur[0], cur[1], scale, o_acc, lse_acc, t, t == comm.world - 1, o, lse)
         if t < comm.world - 1:
             comm.wait(works)
             cur = nxt
-    o = kern.cast(o_acc, 0, 1.0, None, torch.empty((B, S, H, D), device=dev, dtype=q.dtype))
     return o, lse, q_r, k_r
 
 

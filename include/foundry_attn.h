@@ -174,6 +174,18 @@ int fa_fwd_partial(int dtype, int B, int S, int kv_len, int H, int D,
                    const fa_tensor_t* q, const fa_tensor_t* k,
                    const fa_tensor_t* v, const fa_tensor_t* o_blk,
                    float* lse_blk, float scale, void* stream);
+/*
+ * fa_fwd_fold (bf16): fa_fwd_partial and fa_lse_merge in one launch. Folds
+ * the block's attention into the running fp32 (o_acc (B,S,H,D), lse_acc
+ * (B,H,S)) in the kernel's epilogue: step 0 initialises them, later steps
+ * fold into them, and with `last` != 0 the folded result is written as the
+ * final o (bf16) and lse instead (step 0 with `last`: a single block, o_acc
+ * and lse_acc unused).
+ */
+int fa_fwd_fold(int dtype, int B, int S, int kv_len, int H, int D,
+                const fa_tensor_t* q, const fa_tensor_t* k, const fa_tensor_t* v,
+                float* o_acc, float* lse_acc, int step, int last,
+                const fa_tensor_t* o, float* lse, float scale, void* stream);
 int fa_lse_merge(int dtype, int B, int S, int H, int D, float* o_acc,
                  float* lse_acc, const fa_tensor_t* o_blk,
                  const float* lse_blk, int first, void* stream);

@@ -53,6 +53,25 @@ class FakeRingKernels:
         o_blk.copy_((p @ vd).permute(0, 2, 1, 3))
         lse_blk.copy_(lse)
 
+    def fwd_fold(self, q, k, v, scale, o_acc, lse_acc, step, last, o, lse):
+        """fa_fwd_fold: a block folded into (o_acc, lse_acc); the last writes o, lse."""
+        B, S, H, D = q.shape
+        o_blk = torch.empty((B, S, H, D), dtype=torch.float64)
+        lse_blk = torch.empty((B, H, S), dtype=torch.float64)
+        self.fwd_partial(q, k, v, scale, o_blk, lse_blk)
+        if step == 0 and last:
+            o.copy_(o_blk)
+            lse.copy_(lse_blk)
+            return
+        if step == 0:
+            o_acc.copy_(o_blk)
+            lse_acc.copy_(lse_blk)
+            return
+        self.lse_merge(o_acc, lse_acc, o_blk, lse_blk, False)
+        if last:
+            o.copy_(o_acc)
+            lse.copy_(lse_acc)
+
     def lse_merge(self, o_acc, lse_acc, o_blk, lse_blk, first):
         self.calls.append("lse_merge")
         if first:
