@@ -62,6 +62,11 @@ SIGNATURES = {
                                C.c_size_t, _T, _T, _T, _F, _T, _T, _T, C.c_float, _R,
                                C.c_void_p, C.c_size_t, C.c_void_p]),
     "fa_bwd_saved_workspace_bytes": (C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]),
+    "fa_qk_norm_rope_fwd": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _T, _T,
+                                      C.c_void_p, C.c_void_p, C.c_float, _R, _T, C.c_void_p]),
+    "fa_qk_norm_rope_bwd": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _T, _T,
+                                      C.c_void_p, C.c_void_p, C.c_float, _R, _T, _T, _T, _F, _F,
+                                      C.c_void_p]),
     "fa_rope_apply": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _T, _T, _R, C.c_int,
                                 C.c_void_p]),
     "fa_fwd_partial": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _T, _T, _T,

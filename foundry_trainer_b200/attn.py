@@ -100,3 +100,55 @@ class _Op3(torch.autograd.Function):
 def apply_op3(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, op: AttnBwd) -> torch.Tensor:
     """`q.apply_op3(&k, &v, op)`: forward now, op.bwd under autograd."""
     return _Op3.apply(q, k, v, op)
+
+
+class _JointAttention(torch.autograd.Function):
+    """The double block's attention with its fused prologue (see JointAttention)."""
+
+    @staticmethod
+    def forward(ctx, q_t, k_t, v_t, q_i, k_i, v_i, wq_t, wk_t, wq_i, wk_i, rope, eps, scale):
+        T = q_t.shape[1]
+        q_j = ops.qk_norm_rope(q_t, q_i, wq_t, wq_i, rope, eps=eps)
+        k_j = ops.qk_norm_rope(k_t, k_i, wk_t, wk_i, rope, eps=eps)
+        v_j = ops.qk_norm_rope(v_t, v_i, None, None, None)  # concatenation only
+        o_j, lse = ops.attn_fwd(q_j, k_j, v_j, scale=scale)
+        ctx.save_for_backward(q_t, k_t, q_i, k_i, wq_t, wk_t, wq_i, wk_i, q_j, k_j, v_j, o_j, lse)
+        ctx.rope, ctx.eps, ctx.scale, ctx.T = rope, eps, scale, T
+        # the narrow of lib.rs:367-368: views of the joint output
+        return o_j[:, :T], o_j[:, T:]
+
+    @staticmethod
+    def backward(ctx, do_t, do_i):
+        (q_t, k_t, q_i, k_i, wq_t, wk_t, wq_i, wk_i, q_j, k_j, v_j, o_j,
+         lse) = ctx.saved_tensors
+        T = ctx.T
+        do_j = ops.qk_norm_rope(do_t.contiguous(), do_i.contiguous(), None, None, None)
+        dq_j, dk_j, dv_j = ops.attn_bwd(q_j, k_j, v_j, o_j, do_j, lse, scale=ctx.scale)
+        dq_t, dq_i, dwq_t, dwq_i = ops.qk_norm_rope_bwd(q_t, q_i, wq_t, wq_i, ctx.rope, dq_j,
+                                                        eps=ctx.eps)
+        dk_t, dk_i, dwk_t, dwk_i = ops.qk_norm_rope_bwd(k_t, k_i, wk_t, wk_i, ctx.rope, dk_j,
+                                                        eps=ctx.eps)
+        cast = lambda g, w: g.to(w.dtype) if g is not None else None
+        return (dq_t, dk_t, dv_j[:, :T], dq_i, dk_i, dv_j[:, T:], cast(dwq_t, wq_t),
+                cast(dwk_t, wk_t), cast(dwq_i, wq_i), cast(dwk_i, wk_i), None, None, None)
+
+
+class JointAttention:
+    """Attention of the double-stream block from the two streams'
+    projections, as the reference composes it (lib.rs:326-368):
+    per stream q/k RMSNorm with that stream's weights, axial RoPE with the
+    joint positions, cat([txt, img]), the AttnBwd op, and the txt/img narrow.
+    Here the norm, the rotation and the concatenation are one fused pass
+    (fa_qk_norm_rope_fwd) per tensor writing the joint tensor the attention
+    kernels read; the outputs are views of the joint O. Differentiable in the
+    six projections and the four norm weights. bf16, (B, len, H, 128)."""
+
+    def __init__(self, positions: torch.Tensor, eps: float = ops.NORM_EPS,
+                 scale: Optional[float] = None):
+        self.rope = ops.Rope(positions)
+        self.eps = eps
+        self.scale = scale
+
+    def __call__(self, q_t, k_t, v_t, q_i, k_i, v_i, wq_t, wk_t, wq_i, wk_i):
+        return _JointAttention.apply(q_t, k_t, v_t, q_i, k_i, v_i, wq_t, wk_t, wq_i, wk_i,
+                                     self.rope, self.eps, self.scale)

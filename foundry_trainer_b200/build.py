@@ -30,6 +30,7 @@ NVCC_FLAGS = ARCH + [
 ]
 
 LIB_SOURCES = ["capi.cu", "attn_fwd_sm100.cu", "attn_bwd_sm100.cu", "attn_f32.cu", "misc.cu",
+               "qk_prologue.cu",
                "noalloc.cu"]
 SELFTEST_SOURCES = ["umma_selftest.cu"]
 

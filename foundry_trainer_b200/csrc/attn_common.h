@@ -107,11 +107,24 @@ int launch_lse_merge(int dtype, const AttnShape& sh, float* o_acc,
                      float* lse_acc, const fa_tensor_t* o_blk,
                      const float* lse_blk, int first, cudaStream_t stream);
 
+// QK prologue (qk_prologue.cu): per stream RMSNorm + RoPE into the joint
+// (B, T+I, H, 128) tensor, and its backward (dw_* accumulated, may be null)
+int launch_qk_norm_rope_fwd(int B, int T, int I, int H, const fa_tensor_t* x_txt,
+                            const fa_tensor_t* x_img, const void* w_txt, const void* w_img,
+                            float eps, const fa_rope_t* rope, const fa_tensor_t* y,
+                            cudaStream_t stream);
+int launch_qk_norm_rope_bwd(int B, int T, int I, int H, const fa_tensor_t* x_txt,
+                            const fa_tensor_t* x_img, const void* w_txt, const void* w_img,
+                            float eps, const fa_rope_t* rope, const fa_tensor_t* dy,
+                            const fa_tensor_t* dx_txt, const fa_tensor_t* dx_img, float* dw_txt,
+                            float* dw_img, cudaStream_t stream);
+
 // Host: read-and-clear the device status word of each kernel translation
 // unit (0: no bounded wait expired; -1: unreadable).
 int fwd_device_status();
 int bwd_device_status();
 int f32_device_status();
 int misc_device_status();
+int qkp_device_status();
 
 }  // namespace fa

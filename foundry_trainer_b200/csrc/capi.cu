@@ -254,7 +254,7 @@ int fa_device_status(void) {
   // every translation unit's word is read (and cleared); the first code wins
   int first = 0;
   for (int v : {fwd_device_status(), bwd_device_status(), f32_device_status(),
-                misc_device_status()}) {
+                misc_device_status(), qkp_device_status()}) {
     if (v < 0) return FA_ERR_LAUNCH;
     if (first == 0) first = v;
   }
@@ -451,6 +451,59 @@ int fa_bwd_saved(int dtype, int B, int S, int H, int D, const void* fwd_workspac
   timer_end(stop, st);
   FA_TRY(rc);
   return launch_cast_f32(dtype, sh, dq_acc, dq, scale, rope, 0, st, table, s_pad);
+}
+
+// ------------------------------------------------------------ QK prologue
+static int check_qk_prologue(int dtype, int B, int T, int I, int H, int D,
+                             const fa_tensor_t* x_txt, const fa_tensor_t* x_img,
+                             const void* w_txt, const void* w_img, float eps,
+                             const fa_rope_t* rope) {
+  if (dtype != FA_DTYPE_BF16) return FA_ERR_UNSUPPORTED;
+  if (D != 128) return FA_ERR_UNSUPPORTED;
+  if (B <= 0 || H <= 0 || H > 24 || T < 0 || I < 0 || T + I <= 0) return FA_ERR_INVALID_ARG;
+  if ((int64_t)B * (T + I) * H > (int64_t)1 << 31) return FA_ERR_TOO_LARGE;
+  if (!(eps >= 0.f) || !std::isfinite(eps)) return FA_ERR_INVALID_ARG;
+  if (rope != nullptr && (rope->axis_dim != 32 || rope->n_axes != 4)) return FA_ERR_UNSUPPORTED;
+  FA_TRY(check_rope(rope, D));
+  // weights: both streams' (RMSNorm) or none (rotation and concatenation only)
+  const bool norm = (T > 0 ? w_txt : w_img) != nullptr;
+  if (T > 0) {
+    FA_TRY(check_tensor(x_txt, 2, true));
+    if ((w_txt != nullptr) != norm) return FA_ERR_INVALID_ARG;
+    if (norm && reinterpret_cast<uintptr_t>(w_txt) % 16 != 0) return FA_ERR_ALIGNMENT;
+  }
+  if (I > 0) {
+    FA_TRY(check_tensor(x_img, 2, true));
+    if ((w_img != nullptr) != norm) return FA_ERR_INVALID_ARG;
+    if (norm && reinterpret_cast<uintptr_t>(w_img) % 16 != 0) return FA_ERR_ALIGNMENT;
+  }
+  return FA_OK;
+}
+
+int fa_qk_norm_rope_fwd(int dtype, int B, int T, int I, int H, int D,
+                        const fa_tensor_t* x_txt, const fa_tensor_t* x_img,
+                        const void* w_txt, const void* w_img, float eps,
+                        const fa_rope_t* rope, const fa_tensor_t* y, void* stream) {
+  FA_TRY(check_qk_prologue(dtype, B, T, I, H, D, x_txt, x_img, w_txt, w_img, eps, rope));
+  FA_TRY(check_tensor(y, 2, true));
+  FA_TRY(check_sm100());
+  return launch_qk_norm_rope_fwd(B, T, I, H, x_txt, x_img, w_txt, w_img, eps, rope, y,
+                                 reinterpret_cast<cudaStream_t>(stream));
+}
+
+int fa_qk_norm_rope_bwd(int dtype, int B, int T, int I, int H, int D,
+                        const fa_tensor_t* x_txt, const fa_tensor_t* x_img,
+                        const void* w_txt, const void* w_img, float eps,
+                        const fa_rope_t* rope, const fa_tensor_t* dy,
+                        const fa_tensor_t* dx_txt, const fa_tensor_t* dx_img,
+                        float* dw_txt, float* dw_img, void* stream) {
+  FA_TRY(check_qk_prologue(dtype, B, T, I, H, D, x_txt, x_img, w_txt, w_img, eps, rope));
+  FA_TRY(check_tensor(dy, 2, true));
+  if (T > 0) FA_TRY(check_tensor(dx_txt, 2, true));
+  if (I > 0) FA_TRY(check_tensor(dx_img, 2, true));
+  FA_TRY(check_sm100());
+  return launch_qk_norm_rope_bwd(B, T, I, H, x_txt, x_img, w_txt, w_img, eps, rope, dy, dx_txt,
+                                 dx_img, dw_txt, dw_img, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int fa_rope_apply(int dtype, int B, int S, int H, int D, const fa_tensor_t* x,

@@ -162,6 +162,70 @@ def rope_apply(x: torch.Tensor, rope: Rope, *, inverse: bool = False, out=None, 
     return out
 
 
+NORM_EPS = 1e-6  # lib.rs:26
+
+
+def qk_norm_rope(x_txt: Optional[torch.Tensor], x_img: Optional[torch.Tensor],
+                 w_txt: Optional[torch.Tensor], w_img: Optional[torch.Tensor],
+                 rope: Optional[Rope], *, eps: float = NORM_EPS,
+                 out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """The joint block's fused q/k prologue (fa_qk_norm_rope_fwd): per stream
+    rms_norm with its weight (lib.rs:45-58), apply_rope with the joint
+    positions (lib.rs:122-129), written text-then-image into one
+    (B, T+I, H, 128) tensor (the cat of lib.rs:363-365). Either stream may
+    be None; bf16."""
+    xs = [x for x in (x_txt, x_img) if x is not None]
+    if not xs:
+        raise ValueError("at least one stream is required")
+    t4 = as_bshd(x_txt) if x_txt is not None else None
+    i4 = as_bshd(x_img) if x_img is not None else None
+    B, _, H, D = as_bshd(xs[0]).shape
+    T = t4.shape[1] if t4 is not None else 0
+    I = i4.shape[1] if i4 is not None else 0
+    if out is None:
+        out = torch.empty((B, T + I, H, D), device=xs[0].device, dtype=xs[0].dtype)
+    r = rope.c_struct() if rope is not None else None
+    dt_ = desc(t4) if t4 is not None else None
+    di_ = desc(i4) if i4 is not None else None
+    do_ = desc(out)
+    check(_lib.load().fa_qk_norm_rope_fwd(
+        _dtype_code(xs[0]), B, T, I, H, D, _ref(dt_), _ref(di_),
+        w_txt.data_ptr() if w_txt is not None else None,
+        w_img.data_ptr() if w_img is not None else None, float(eps), _ref(r), C.byref(do_),
+        _stream_ptr(stream)), "fa_qk_norm_rope_fwd")
+    return out
+
+
+def qk_norm_rope_bwd(x_txt, x_img, w_txt, w_img, rope: Optional[Rope], dy: torch.Tensor, *,
+                     eps: float = NORM_EPS, dw_txt: Optional[torch.Tensor] = None,
+                     dw_img: Optional[torch.Tensor] = None, stream=None):
+    """Gradients of qk_norm_rope: (dx_txt, dx_img, dw_txt, dw_img). The weight
+    gradients are fp32 and ADDED to dw_* when given (zeros otherwise)."""
+    t4 = as_bshd(x_txt) if x_txt is not None else None
+    i4 = as_bshd(x_img) if x_img is not None else None
+    d4 = as_bshd(dy)
+    B, S, H, D = d4.shape
+    T = t4.shape[1] if t4 is not None else 0
+    I = i4.shape[1] if i4 is not None else 0
+    dev = dy.device
+    dx_t = torch.empty_like(x_txt) if x_txt is not None else None
+    dx_i = torch.empty_like(x_img) if x_img is not None else None
+    if x_txt is not None and dw_txt is None:
+        dw_txt = torch.zeros(D, device=dev, dtype=torch.float32)
+    if x_img is not None and dw_img is None:
+        dw_img = torch.zeros(D, device=dev, dtype=torch.float32)
+    r = rope.c_struct() if rope is not None else None
+    ds = [desc(x) if x is not None else None for x in (t4, i4, d4, dx_t, dx_i)]
+    check(_lib.load().fa_qk_norm_rope_bwd(
+        _dtype_code(dy), B, T, I, H, D, _ref(ds[0]), _ref(ds[1]),
+        w_txt.data_ptr() if w_txt is not None else None,
+        w_img.data_ptr() if w_img is not None else None, float(eps), _ref(r), C.byref(ds[2]),
+        _ref(ds[3]), _ref(ds[4]), dw_txt.data_ptr() if dw_txt is not None else None,
+        dw_img.data_ptr() if dw_img is not None else None, _stream_ptr(stream)),
+        "fa_qk_norm_rope_bwd")
+    return dx_t, dx_i, dw_txt, dw_img
+
+
 def device_status() -> int:
     """Reads and clears the device status word (0 when no bounded wait expired)."""
     return int(_lib.load().fa_device_status())

@@ -143,6 +143,32 @@ int fa_rope_apply(int dtype, int B, int S, int H, int D, const fa_tensor_t* x,
                   void* stream);
 
 /*
+ * Q/K prologue of the joint block, fused (bf16, head dim 128): for each
+ * stream — text rows [0, T) from x_txt (B, T, H, 128), image rows [T, T+I)
+ * from x_img (B, I, H, 128), any strides with a contiguous head dim — the
+ * reference's rms_norm with that stream's weight (lib.rs:45-58; w_* are
+ * (128,) bf16, eps as NORM_EPS lib.rs:26), then apply_rope with the joint
+ * positions (lib.rs:122-129, rope may be NULL), written into the joint
+ * y (B, T+I, H, 128): the cat([txt, img]) of lib.rs:363-365 costs nothing.
+ * Either stream may be empty (T = 0 is the single-stream block). With both
+ * weights NULL there is no normalisation: the rows are only rotated (rope
+ * non-NULL) and concatenated — the joint v, or dO from the two streams'
+ * output gradients.
+ * The backward maps dy (gradient of y) to dx_txt, dx_img and ADDS the norm
+ * weights' gradients into dw_txt, dw_img (fp32 (128,), NULL to skip).
+ */
+int fa_qk_norm_rope_fwd(int dtype, int B, int T, int I, int H, int D,
+                        const fa_tensor_t* x_txt, const fa_tensor_t* x_img,
+                        const void* w_txt, const void* w_img, float eps,
+                        const fa_rope_t* rope, const fa_tensor_t* y, void* stream);
+int fa_qk_norm_rope_bwd(int dtype, int B, int T, int I, int H, int D,
+                        const fa_tensor_t* x_txt, const fa_tensor_t* x_img,
+                        const void* w_txt, const void* w_img, float eps,
+                        const fa_rope_t* rope, const fa_tensor_t* dy,
+                        const fa_tensor_t* dx_txt, const fa_tensor_t* dx_img,
+                        float* dw_txt, float* dw_img, void* stream);
+
+/*
  * Sequence-parallel (ring) building blocks. They have no counterpart in the
  * reference, which is single-GPU (it has no collectives); they let a host
  * driver rotate K/V shards between ranks and fold each block into the local

@@ -24,6 +24,10 @@ Outputs (float32 arrays; bf16 values are exact in float32):
       normalised activations and weights, and `pos` the generator's axial
       positions (gen_block.py:316-326, including the single block's
       image-then-text order).
+  qk_norm_rope_fixture_fp32.npz, qk_norm_rope_fixture_bf16.npz
+      x (the projection), w (the q-norm weight), pos, y = apply_rope(rms_norm(
+      x, w)) and, for a seeded upstream gradient dy, dx and dw from torch
+      autograd through the generator's ops (gen_block.py:65-69, 103-109).
   attn_rope_fixture_fp32.npz
       q, k, v (pre-rotation), dout, pos, and o, dq, dk, dv from the
       generator's own `apply_rope` + `attention` + torch autograd
@@ -102,7 +106,27 @@ def main(ref_root: str) -> None:
             rope[f"{name}_pre"] = pre.float().numpy()
             rope[f"{name}_pos"] = pos.numpy().astype(np.float32)
             rope[f"{name}_post"] = post.float().numpy()
+            # the RMSNorm input (the projection) and weight: with pos and
+            # post, a golden of the fused QK-RMSNorm + RoPE prologue
+            rope[f"{name}_h"] = x.float().numpy()
+            rope[f"{name}_w"] = w[normw].float().numpy()
         np.savez_compressed(HERE / f"rope_fixture_{tag}.npz", **rope)
+
+        # backward of the QK prologue: torch autograd through the generator's
+        # rms_norm + apply_rope (gen_block.py:65-69, 103-109) for the double
+        # block's image q case, with a seeded upstream gradient
+        x, normw, pos, _ = cases["dimg_q"]
+        cos, sin = gb.rope_tables(pos, cfg["rope_axes"], cfg["rope_theta"])
+        xv = x.detach().clone().requires_grad_(True)
+        wv = w[normw].detach().clone().requires_grad_(True)
+        y = gb.apply_rope(gb.rms_norm(xv, wv, eps), cos, sin, cfg["rope_axes"])
+        gen = torch.Generator().manual_seed(99)
+        dy = torch.randn(y.shape, generator=gen).to(y.dtype)
+        dx, dw = torch.autograd.grad(y, [xv, wv], dy)
+        np.savez_compressed(HERE / f"qk_norm_rope_fixture_{tag}.npz",
+                            x=x.float().numpy(), w=w[normw].float().numpy(),
+                            pos=pos.numpy().astype(np.float32), y=y.detach().float().numpy(),
+                            dy=dy.float().numpy(), dx=dx.float().numpy(), dw=dw.float().numpy())
 
     # end-to-end rotation-inside-the-op golden (fp32), seeded
     gen = torch.Generator().manual_seed(1234)

@@ -81,3 +81,29 @@ def test_max_rel_definition():
     ref = np.array([1.0, -4.0, 2.0])
     ours = np.array([1.1, -4.0, 2.0])
     assert abs(orc.max_rel(ours, ref) - 0.1 / 4.0) < 1e-12
+
+
+@pytest.mark.parametrize("tag,tol", [("fp32", 2e-6), ("bf16", 1e-4)])
+def test_oracle_qk_norm_rope_matches_fixture(golden_dir, tag, tol):
+    """Fused prologue rms_norm + apply_rope from the projection, against the
+    reference's recorded post-RoPE q/k of both blocks."""
+    g = _load(golden_dir, f"rope_fixture_{tag}.npz")
+    dt = "f32" if tag == "fp32" else "bf16"
+    for c in sorted({k.rsplit("_", 1)[0] for k in g}):
+        y = orc.qk_norm_rope(g[f"{c}_h"], g[f"{c}_w"], 1e-6, g[f"{c}_pos"], dt)
+        assert orc.max_rel(y, g[f"{c}_post"]) <= tol, c
+        n, _ = orc.rms_norm(g[f"{c}_h"], g[f"{c}_w"], 1e-6, dt)
+        assert orc.max_rel(n, g[f"{c}_pre"]) <= tol, c
+
+
+@pytest.mark.parametrize("tag,tol", [("fp32", 1e-6), ("bf16", 1e-2)])
+def test_oracle_qk_norm_rope_grad_matches_fixture(golden_dir, tag, tol):
+    """Backward of the prologue against torch autograd through the
+    generator's rms_norm + apply_rope."""
+    g = _load(golden_dir, f"qk_norm_rope_fixture_{tag}.npz")
+    dt = "f32" if tag == "fp32" else "bf16"
+    y = orc.qk_norm_rope(g["x"], g["w"], 1e-6, g["pos"], dt)
+    assert orc.max_rel(y, g["y"]) <= tol
+    dx, dw = orc.qk_norm_rope_grad(g["x"], g["w"], 1e-6, g["pos"], g["dy"], dt)
+    assert orc.max_rel(dx, g["dx"]) <= tol
+    assert orc.max_rel(dw, g["dw"]) <= tol
