@@ -8,9 +8,14 @@ synthetic batch of the named configuration, inputs resident in HBM. With N > 1
 (launched under torch.distributed.run, one rank per GPU) every rank runs its
 own batch x head partition of the workload with no collective on the data
 path (weak scaling); the timed region is bracketed by a barrier and a device
-synchronise, and the maximum time over ranks is reported. `--config c5` runs
-the long-sequence case as a ring instead: one sequence of 16896 rows sharded
-over the ranks, K/V passed round an NCCL ring (strong scaling).
+synchronise, and the maximum time over ranks is reported. `--config c4` splits
+its batch of 8 sequences over the ranks instead (strong scaling, still no
+cross-GPU traffic). `--config c5` runs
+the long-sequence case sequence-parallel instead: one sequence of 16896 rows
+sharded over the ranks (strong scaling); the K/V shards and the dK/dV
+contributions cross NVLink through peer memory (`--transport peer`, the
+default: copy-engine pulls, stores from the backward's epilogue, device
+barriers) or an NCCL send/recv ring (`--transport nccl`).
 
 Rank 0 prints one JSON line: the metric (TFLOP/s, FlashAttention accounting
 14*B*H*S^2*D), the roofline of the dominant kernel (the backward kernel,
@@ -193,6 +198,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="c2", choices=["c1", "c2", "c4", "c5"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--transport", default="peer", choices=["peer", "nccl"],
+                    help="c5 exchange: peer memory (copy-engine pulls, peer stores, device "
+                         "barriers) or NCCL send/recv round a ring")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--ncu-case", action="store_true",
@@ -227,6 +235,8 @@ def main():
                                 device_id=dev)
 
     ring_mode = cfg.name == "c5"
+    batch_mode = cfg.name == "c4"
+    b_loc = cfg.B
     pos_full = configs.positions(cfg.txt, cfg.grid)
     if ring_mode:
         # strong scaling: one sequence sharded along S over the ranks, K/V
@@ -238,28 +248,51 @@ def main():
         sl = slice(rank * n_loc, (rank + 1) * n_loc)
         q, k, v, d_o = (t[:, sl].contiguous().to(dev) for t in configs.make_inputs(cfg))
         pos = pos_full[sl].contiguous().to(dev)
-        comm, kern = ring.RingComm(), ring.RingKernels()
         scale = ops.default_scale(cfg.D)
+        if args.transport == "peer":
+            from foundry_trainer_b200 import peer
+            ex, pkern = peer.PeerExchange(cfg.B, n_loc, cfg.H, cfg.D), peer.PeerKernels()
 
-        def make_step(q, k, v, d_o):
-            outs = {}
+            def make_step(q, k, v, d_o):
+                outs = {}
 
-            def step():
-                o_, lse_, q_r, k_r = ring.ring_fwd(q, k, v, pos, scale, comm, kern)
-                outs["o"] = o_
-                outs["dq"], outs["dk"], outs["dv"] = ring.ring_bwd(q_r, k_r, v, o_, d_o, lse_,
-                                                                    pos, scale, comm, kern)
-            return step, outs
+                def step():
+                    o_, lse_, q_r, k_all, v_all = peer.peer_fwd(q, k, v, pos, scale, ex, pkern)
+                    outs["o"] = o_
+                    outs["dq"], outs["dk"], outs["dv"] = peer.peer_bwd(
+                        q_r, k_all, v_all, o_, d_o, lse_, pos, scale, ex, pkern)
+                return step, outs
+        else:
+            comm, kern = ring.RingComm(), ring.RingKernels()
+
+            def make_step(q, k, v, d_o):
+                outs = {}
+
+                def step():
+                    o_, lse_, q_r, k_r = ring.ring_fwd(q, k, v, pos, scale, comm, kern)
+                    outs["o"] = o_
+                    outs["dq"], outs["dk"], outs["dv"] = ring.ring_bwd(q_r, k_r, v, o_, d_o, lse_,
+                                                                        pos, scale, comm, kern)
+                return step, outs
     else:
-        # weak scaling: each rank owns one batch x head partition of cfg's size
         n_loc = cfg.S
-        q, k, v, d_o = (t.to(dev) for t in configs.make_inputs(cfg))
+        if batch_mode:
+            # strong scaling: the B sequences of the batch split over the
+            # ranks (B / N each), no cross-GPU traffic
+            if cfg.B % world != 0:
+                raise SystemExit(f"{cfg.name}: B={cfg.B} does not split over {world} ranks")
+            b_loc = cfg.B // world
+            bl = slice(rank * b_loc, (rank + 1) * b_loc)
+            q, k, v, d_o = (t[bl].contiguous().to(dev) for t in configs.make_inputs(cfg))
+        else:
+            # weak scaling: each rank owns a whole problem of cfg's size
+            q, k, v, d_o = (t.to(dev) for t in configs.make_inputs(cfg))
         pos = pos_full.to(dev)
         rope = ops.Rope(pos)
 
         def make_step(q, k, v, d_o):
             o = torch.empty_like(q)
-            lse = torch.empty((cfg.B, cfg.H, cfg.S), device=dev, dtype=torch.float32)
+            lse = torch.empty((q.shape[0], cfg.H, cfg.S), device=dev, dtype=torch.float32)
             dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
             outs = {"o": o, "dq": dq, "dk": dk, "dv": dv}
 
@@ -281,6 +314,8 @@ def main():
         if ops.device_status() != 0:
             raise RuntimeError("device-side bounded wait expired")
         print("ncu case ok", flush=True)
+        if ring_mode and args.transport == "peer":
+            ex.close()
         if world > 1:
             dist.destroy_process_group()
         return
@@ -355,17 +390,19 @@ def main():
     step_ms_max, bwd_ms, fwd_ms = t.tolist()
 
     # whole-job FLOPs per step: every rank's own problem (weak), or the one
-    # sharded sequence (ring, strong)
-    flops_step = cfg.flops_fwd_bwd() * (1 if ring_mode else world)
+    # sharded sequence or batch (ring / batch split, strong)
+    strong = ring_mode or batch_mode
+    flops_step = cfg.flops_fwd_bwd() * (1 if strong else world)
     value = K * flops_step / (step_ms_max / 1e3) / 1e12
     # per kernel launch: the whole local problem, or one ring block
-    blk = 4.0 * cfg.B * cfg.H * n_loc * n_loc * cfg.D
+    blk = 4.0 * b_loc * cfg.H * n_loc * n_loc * cfg.D
 
     peaks = _peaks()
     timed_seconds = step_ms_max / 1e3
     peak_kind = "bf16_sustained" if timed_seconds > 2.0 else "bf16"
     peak = peaks[peak_kind]
-    bwd_flops = 2.5 * blk
+    # the peer path's backward is one launch over all W shards' keys
+    bwd_flops = 2.5 * blk * (world if ring_mode and args.transport == "peer" else 1)
     achieved = bwd_flops / (bwd_ms / 1e3) / 1e12
     traffic = None
     tf = ROOT / "profiles" / "traffic.json"
@@ -456,7 +493,9 @@ def main():
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "ms_per_step": te.item() / K,
                "path": ("ring.ring_fwd + ring.ring_bwd (C ABI fa_fwd_partial/fa_bwd_partial "
-                        "round an NCCL ring)" if ring_mode else
+                        "round an NCCL ring)" if ring_mode and args.transport == "nccl" else
+                        "peer.peer_fwd + peer.peer_bwd (C ABI fa_fwd_fold/fa_merge_f32/"
+                        "fa_bwd_scatter/fa_reduce_cast_f32 over peer memory)" if ring_mode else
                         "ops.attn_fwd + ops.attn_bwd (C ABI fa_fwd/fa_bwd_saved)") +
                        " per rank; every step copies its pinned host q,k,v,dO in and o,dq,dk,dv "
                        "out; copies of the neighbouring steps overlap the compute on separate "
@@ -469,12 +508,23 @@ def main():
                "sample": f"{heads} of {cfg.H} heads of {cfg.name} fwd+bwd with RoPE, fp32 numpy "
                          f"oracle, {secs:.1f} s"}
 
+    if ring_mode and args.transport == "peer":
+        ex.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return
-    if ring_mode:
+    if ring_mode and args.transport == "peer":
+        # fwd: rope q, rope k, W folds (+ merge and barrier when W > 1);
+        # bwd: prepare, one scatter launch, reduce-cast, dQ cast (+ barrier)
+        launches_per_step = 2 + world + 4 + (3 if world > 1 else 0)
+        workload = (f"{cfg.name}: B={cfg.B} H={cfg.H} S={cfg.S} ({cfg.txt} text + "
+                    f"{cfg.grid}x{cfg.grid} image) D={cfg.D}, one sequence sharded "
+                    f"{n_loc} rows per rank, non-causal, axial RoPE")
+        parallelism = (f"sequence-parallel x{world} over peer memory (copy-engine K/V pulls, "
+                       f"dK/dV rows stored into the owners by the backward's epilogue)")
+    elif ring_mode:
         # fwd: rope q, rope k, W blocks + W merges, O cast; bwd: prepare,
         # W blocks, W-1 accumulator adds, 3 casts
         launches_per_step = 4 * world + 6
@@ -484,17 +534,23 @@ def main():
         parallelism = f"sequence ring x{world} (NCCL send/recv of K,V and fp32 dK,dV)"
     else:
         launches_per_step = 5  # rope q,k (+ table) + fwd; delta (+ dQ clear) + bwd + dQ finish
-        workload = (f"{cfg.name}: B={cfg.B} H={cfg.H} S={cfg.S} "
-                    f"({cfg.txt} text + {cfg.grid}x{cfg.grid} image) D={cfg.D} "
-                    f"per rank, non-causal, axial RoPE inside the op")
-        parallelism = f"batch-sharded x{world}, no collective on the data path"
+        if batch_mode:
+            workload = (f"{cfg.name}: B={cfg.B} H={cfg.H} S={cfg.S} "
+                        f"({cfg.txt} text + {cfg.grid}x{cfg.grid} image) D={cfg.D}, the batch "
+                        f"split {b_loc} sequences per rank, non-causal, axial RoPE inside the op")
+            parallelism = f"batch split x{world} (B={b_loc} per rank), no collective"
+        else:
+            workload = (f"{cfg.name}: B={cfg.B} H={cfg.H} S={cfg.S} "
+                        f"({cfg.txt} text + {cfg.grid}x{cfg.grid} image) D={cfg.D} "
+                        f"per rank, non-causal, axial RoPE inside the op")
+            parallelism = f"batch-sharded x{world}, no collective on the data path"
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": args.warmup, "ms_per_step": step_ms_max / K, "higher_is_better": True,
-        "scaling": "strong" if ring_mode else "weak", "vs_baseline": None, "dtype": "bf16",
+        "scaling": "strong" if strong else "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded torch.Generator, q,k,v ~ 0.5*N(0,1), dO ~ N(0,1))",
         "config": {"workload": workload,
-                   "per_rank_B": cfg.B, "H": cfg.H, "S": cfg.S, "S_per_rank": n_loc, "D": cfg.D,
+                   "per_rank_B": b_loc, "H": cfg.H, "S": cfg.S, "S_per_rank": n_loc, "D": cfg.D,
                    "l2": "flushed between timed steps (256 MB write outside the step events)",
                    "parallelism": parallelism},
         "roofline": roofline,

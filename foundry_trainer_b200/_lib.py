@@ -45,6 +45,10 @@ class fa_rope_t(C.Structure):
                 ("theta", C.c_float)]
 
 
+class fa_peer_handle_t(C.Structure):
+    _fields_ = [("bytes", C.c_ubyte * 64)]
+
+
 _T = C.POINTER(fa_tensor_t)
 _R = C.POINTER(fa_rope_t)
 _F = C.c_void_p  # float* (device)
@@ -84,6 +88,22 @@ SIGNATURES = {
                               C.c_float, _R, C.c_void_p]),
     "fa_bwd_noalloc": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, _T, _T, _T, _T, _T, _F, _T, _T,
                                  _T, C.c_float, C.c_void_p]),
+    "fa_peer_flags_bytes": (C.c_size_t, []),
+    "fa_peer_alloc": (C.c_int, [C.c_size_t, C.POINTER(C.c_void_p), C.POINTER(fa_peer_handle_t)]),
+    "fa_peer_open": (C.c_int, [C.POINTER(fa_peer_handle_t), C.POINTER(C.c_void_p)]),
+    "fa_peer_close": (C.c_int, [C.c_void_p]),
+    "fa_peer_free": (C.c_int, [C.c_void_p]),
+    "fa_copy_2d": (C.c_int, [C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t, C.c_size_t,
+                             C.c_size_t, C.c_void_p]),
+    "fa_peer_barrier": (C.c_int, [C.c_int, C.c_int, C.POINTER(C.c_void_p), C.c_int, C.c_double,
+                                  C.c_void_p]),
+    "fa_bwd_scatter": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _T, _T, _T,
+                                 _T, _F, _F, _F, C.c_int, C.c_int, C.POINTER(C.c_void_p),
+                                 C.POINTER(C.c_void_p), C.c_float, C.c_void_p]),
+    "fa_reduce_cast_f32": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _F, _F, C.c_int,
+                                     C.c_int64, _T, _T, C.c_float, _R, C.c_void_p]),
+    "fa_merge_f32": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _F, _F, _F, _F, _T, _F,
+                               C.c_void_p]),
     "fa_timing_enable": (C.c_int, [C.c_int]),
     "fa_timing_read": (C.c_int, [C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_int)]),
     "fa_status_string": (C.c_char_p, [C.c_int]),

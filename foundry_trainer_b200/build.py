@@ -29,7 +29,7 @@ NVCC_FLAGS = ARCH + [
     "--expt-relaxed-constexpr", "-I", str(ROOT / "include"), "-I", str(CSRC),
 ]
 
-LIB_SOURCES = ["capi.cu", "attn_fwd_sm100.cu", "attn_bwd_sm100.cu", "attn_f32.cu", "misc.cu",
+LIB_SOURCES = ["capi.cu", "attn_fwd_sm100.cu", "attn_bwd_sm100.cu", "attn_f32.cu", "misc.cu", "peer.cu",
                "qk_prologue.cu",
                "noalloc.cu"]
 SELFTEST_SOURCES = ["umma_selftest.cu"]

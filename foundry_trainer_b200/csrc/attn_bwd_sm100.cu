@@ -85,9 +85,15 @@ struct Params {
   float scale, scale_log2;
   const float* lse2_pad;    // (B, H, s_pad): LSE * log2(e), +inf padding
   const float* delta_pad;   // (B, H, s_pad): rowsum(dO*O), 0 padding
-  // dK / dV output: bf16 strided tensors (acc 0), or fp32 (B, kv_len, H, D)
-  // buffers that the result is added to (acc 1) or stored in (acc 2)
+  // dK / dV output: bf16 strided tensors (acc 0), fp32 (B, kv_len, H, D)
+  // buffers that the result is added to (acc 1) or stored in (acc 2), or
+  // fp32 rows stored per key segment (acc 3: row j to seg_dk[j / seg] at
+  // local row j % seg, (B, seg, H, D) each; a segment may be a peer GPU's
+  // memory, written with plain stores)
   int acc;
+  int seg;
+  float* seg_dk[FA_PEER_MAX];
+  float* seg_dv[FA_PEER_MAX];
   __nv_bfloat16* dk;
   int64_t dks_b, dks_s, dks_h;
   __nv_bfloat16* dv;
@@ -128,8 +134,17 @@ __device__ __forceinline__ void store_chunk32(const Params& p, bool is_dk, int b
                                               int key, int h, int col0,
                                               const float* v) {
   if (p.acc) {
-    float* dst = (is_dk ? p.dk_acc : p.dv_acc) +
-                 (((int64_t)b * p.kv_len + key) * p.H + h) * 128 + col0;
+    float* base;
+    int64_t row;
+    if (p.acc == 3) {
+      const int o = key / p.seg;
+      base = is_dk ? p.seg_dk[o] : p.seg_dv[o];
+      row = (int64_t)b * p.seg + (key - o * p.seg);
+    } else {
+      base = is_dk ? p.dk_acc : p.dv_acc;
+      row = (int64_t)b * p.kv_len + key;
+    }
+    float* dst = base + (row * p.H + h) * 128 + col0;
     float4* d4 = reinterpret_cast<float4*>(dst);
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
@@ -191,7 +206,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                 const __grid_constant__ CUtensorMap tm_k,
                 const __grid_constant__ CUtensorMap tm_v,
-                const __grid_constant__ CUtensorMap tm_do, Params p) {
+                const __grid_constant__ CUtensorMap tm_do, const __grid_constant__ Params p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc);
@@ -532,7 +547,7 @@ int launch_attn_bwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
                          const fa_tensor_t* dk, const fa_tensor_t* dv,
                          float* dk_acc, float* dv_acc, int accumulate, float scale,
                          const fa_rope_t* rope, const float2* rope_table,
-                         cudaStream_t stream) {
+                         cudaStream_t stream, const BwdScatter* scatter) {
   if (rope != nullptr && (rope->axis_dim != 32 || rope->n_axes != 4))
     return FA_ERR_UNSUPPORTED;  // the dK epilogue un-rotates 32-wide axes
   if (rope != nullptr && rope_table == nullptr)
@@ -554,6 +569,16 @@ int launch_attn_bwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
   p.lse2_pad = lse2_pad;
   p.delta_pad = delta_pad;
   p.acc = (dk_acc != nullptr) ? (accumulate ? 1 : 2) : 0;
+  p.seg = 1;
+  for (int i = 0; i < FA_PEER_MAX; ++i) p.seg_dk[i] = p.seg_dv[i] = nullptr;
+  if (scatter != nullptr) {
+    p.acc = 3;
+    p.seg = scatter->seg;
+    for (int i = 0; i < scatter->n; ++i) {
+      p.seg_dk[i] = scatter->dk[i];
+      p.seg_dv[i] = scatter->dv[i];
+    }
+  }
   p.dk = dk ? reinterpret_cast<__nv_bfloat16*>(dk->data) : nullptr;
   p.dks_b = dk ? dk->stride_b : 0;
   p.dks_s = dk ? dk->stride_s : 0;

@@ -53,6 +53,14 @@ int launch_attn_fwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
                          cudaStream_t stream, int merge = 0, float* o_acc = nullptr,
                          float* lse_acc = nullptr);
 
+// dK/dV rows stored per key segment: row j to dk[j / seg], dv[j / seg] at
+// local row j % seg (fp32 contiguous (B, seg, H, D) each; peers' memory allowed)
+struct BwdScatter {
+  int seg, n;
+  float* dk[FA_PEER_MAX];
+  float* dv[FA_PEER_MAX];
+};
+
 int launch_attn_bwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
                          const fa_tensor_t* k, const fa_tensor_t* v,
                          const fa_tensor_t* d_o, const float* lse2_pad,
@@ -60,7 +68,7 @@ int launch_attn_bwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
                          const fa_tensor_t* dk, const fa_tensor_t* dv,
                          float* dk_acc, float* dv_acc, int accumulate, float scale,
                          const fa_rope_t* rope, const float2* rope_table,
-                         cudaStream_t stream);
+                         cudaStream_t stream, const BwdScatter* scatter = nullptr);
 
 // fp32 SIMT kernels (exact path)
 int launch_attn_fwd_f32(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
@@ -119,6 +127,19 @@ int launch_qk_norm_rope_bwd(int B, int T, int I, int H, const fa_tensor_t* x_txt
                             const fa_tensor_t* dx_txt, const fa_tensor_t* dx_img, float* dw_txt,
                             float* dw_img, cudaStream_t stream);
 
+// Sequence-parallel exchange (peer.cu): bounded barrier over the ranks' flag
+// blocks, the owner's sum of received dK/dV contributions (dK un-rotated and
+// scaled by alpha), and the merge of two fp32 (O, LSE) partials
+int launch_peer_barrier(int rank, int world, void* const* flags, int channel,
+                        double timeout_s, cudaStream_t stream);
+int launch_reduce_cast(int dtype, const AttnShape& sh, const float* x, const float* x2,
+                       int n_parts, int64_t part_stride, const fa_tensor_t* y,
+                       const fa_tensor_t* y2, float alpha, const fa_rope_t* rope,
+                       cudaStream_t stream);
+int launch_merge2(int dtype, const AttnShape& sh, const float* o_a, const float* lse_a,
+                  const float* o_b, const float* lse_b, const fa_tensor_t* o, float* lse,
+                  cudaStream_t stream);
+
 // Host: read-and-clear the device status word of each kernel translation
 // unit (0: no bounded wait expired; -1: unreadable).
 int fwd_device_status();
@@ -126,5 +147,6 @@ int bwd_device_status();
 int f32_device_status();
 int misc_device_status();
 int qkp_device_status();
+int peer_device_status();
 
 }  // namespace fa

@@ -254,7 +254,7 @@ int fa_device_status(void) {
   // every translation unit's word is read (and cleared); the first code wins
   int first = 0;
   for (int v : {fwd_device_status(), bwd_device_status(), f32_device_status(),
-                misc_device_status(), qkp_device_status()}) {
+                misc_device_status(), qkp_device_status(), peer_device_status()}) {
     if (v < 0) return FA_ERR_LAUNCH;
     if (first == 0) first = v;
   }
@@ -637,6 +637,157 @@ int fa_cast_f32(int dtype, int B, int S, int H, int D, const float* x,
   const int s_pad = x_layout == 1 ? ((S + 127) / 128) * 128 : 0;
   return launch_cast_f32(dtype, AttnShape{B, S, H, D}, x, y, alpha, rope, 0,
                          reinterpret_cast<cudaStream_t>(stream), nullptr, s_pad);
+}
+
+// ------------------------------------------------------------ peer exchange
+
+size_t fa_peer_flags_bytes(void) { return 256; }
+
+int fa_peer_alloc(size_t bytes, void** ptr, fa_peer_handle_t* handle) {
+  if (bytes == 0 || ptr == nullptr || handle == nullptr) return FA_ERR_INVALID_ARG;
+  FA_TRY(check_sm100());
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return record_cuda_error(e);
+  cudaIpcMemHandle_t h;
+  e = cudaMemset(p, 0, bytes);
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return record_cuda_error(e);
+  }
+  static_assert(sizeof(h) == sizeof(handle->bytes), "IPC handle size");
+  std::memcpy(handle->bytes, &h, sizeof(h));
+  *ptr = p;
+  return FA_OK;
+}
+
+int fa_peer_open(const fa_peer_handle_t* handle, void** ptr) {
+  if (handle == nullptr || ptr == nullptr) return FA_ERR_INVALID_ARG;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle->bytes, sizeof(h));
+  void* p = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return record_cuda_error(e);
+  *ptr = p;
+  return FA_OK;
+}
+
+int fa_peer_close(void* ptr) {
+  if (ptr == nullptr) return FA_ERR_INVALID_ARG;
+  return record_cuda_error(cudaIpcCloseMemHandle(ptr));
+}
+
+int fa_peer_free(void* ptr) {
+  if (ptr == nullptr) return FA_ERR_INVALID_ARG;
+  return record_cuda_error(cudaFree(ptr));
+}
+
+int fa_copy_2d(void* dst, size_t dpitch, const void* src, size_t spitch, size_t width,
+               size_t height, void* stream) {
+  if (width == 0 || height == 0) return FA_OK;
+  if (dst == nullptr || src == nullptr || dpitch < width || spitch < width)
+    return FA_ERR_INVALID_ARG;
+  const cudaError_t e = cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, height,
+                                          cudaMemcpyDefault,
+                                          reinterpret_cast<cudaStream_t>(stream));
+  return record_cuda_error(e);
+}
+
+int fa_peer_barrier(int rank, int world, void* const* flags, int channel, double timeout_s,
+                    void* stream) {
+  if (world < 1 || world > FA_PEER_MAX || rank < 0 || rank >= world || flags == nullptr ||
+      channel < 0 || channel >= FA_PEER_CHANNELS || !(timeout_s > 0.0))
+    return FA_ERR_INVALID_ARG;
+  for (int i = 0; i < world; ++i)
+    if (flags[i] == nullptr || reinterpret_cast<uintptr_t>(flags[i]) % 16 != 0)
+      return FA_ERR_INVALID_ARG;
+  if (world == 1) return FA_OK;
+  FA_TRY(check_sm100());
+  return launch_peer_barrier(rank, world, flags, channel, timeout_s,
+                             reinterpret_cast<cudaStream_t>(stream));
+}
+
+int fa_bwd_scatter(int dtype, int B, int S, int kv_len, int H, int D, const fa_tensor_t* q,
+                   const fa_tensor_t* k, const fa_tensor_t* v, const fa_tensor_t* d_o,
+                   const float* lse2_pad, const float* delta_pad, float* dq_acc, int seg,
+                   int n_seg, float* const* dk_seg, float* const* dv_seg, float scale,
+                   void* stream) {
+  FA_TRY(check_shape(dtype, B, S, H, D));
+  if (dtype != FA_DTYPE_BF16) return FA_ERR_UNSUPPORTED;
+  if (kv_len <= 0 || seg <= 0 || n_seg < 1 || n_seg > FA_PEER_MAX ||
+      (int64_t)seg * n_seg < kv_len || (int64_t)seg * (n_seg - 1) >= kv_len)
+    return FA_ERR_INVALID_ARG;
+  if (!(scale > 0.f) || !std::isfinite(scale)) return FA_ERR_INVALID_ARG;
+  for (const fa_tensor_t* t : {q, k, v, d_o}) FA_TRY(check_tensor(t, 2, true));
+  if (!lse2_pad || !delta_pad || !dq_acc || !dk_seg || !dv_seg) return FA_ERR_INVALID_ARG;
+  for (const void* pp : {(const void*)lse2_pad, (const void*)delta_pad, (const void*)dq_acc})
+    if (reinterpret_cast<uintptr_t>(pp) % 16 != 0) return FA_ERR_ALIGNMENT;
+  BwdScatter sc{};
+  sc.seg = seg;
+  sc.n = n_seg;
+  for (int i = 0; i < n_seg; ++i) {
+    if (dk_seg[i] == nullptr || dv_seg[i] == nullptr) return FA_ERR_INVALID_ARG;
+    if (reinterpret_cast<uintptr_t>(dk_seg[i]) % 16 != 0 ||
+        reinterpret_cast<uintptr_t>(dv_seg[i]) % 16 != 0)
+      return FA_ERR_ALIGNMENT;
+    sc.dk[i] = dk_seg[i];
+    sc.dv[i] = dv_seg[i];
+  }
+  FA_TRY(check_sm100());
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  cudaEvent_t stop = timer_begin(FA_TIMER_BWD, st);
+  const int rc = launch_attn_bwd_bf16(AttnShape{B, S, H, D}, kv_len, q, k, v, d_o, lse2_pad,
+                                      delta_pad, dq_acc, nullptr, nullptr, nullptr, nullptr, 0,
+                                      scale, nullptr, nullptr, st, &sc);
+  timer_end(stop, st);
+  return rc;
+}
+
+int fa_reduce_cast_f32(int dtype, int B, int S, int H, int D, const float* x, const float* x2,
+                       int n_parts, int64_t part_stride, const fa_tensor_t* y,
+                       const fa_tensor_t* y2, float alpha, const fa_rope_t* rope,
+                       void* stream) {
+  FA_TRY(check_shape(dtype, B, S, H, D));
+  FA_TRY(check_rope(rope, D));
+  if (D != 128) return FA_ERR_UNSUPPORTED;
+  if (rope != nullptr && (rope->axis_dim != 32 || rope->n_axes != 4)) return FA_ERR_UNSUPPORTED;
+  if (x == nullptr || n_parts < 1 || part_stride < (int64_t)B * S * H * D ||
+      part_stride % 4 != 0 || (y2 != nullptr && x2 == nullptr))
+    return FA_ERR_INVALID_ARG;
+  if (reinterpret_cast<uintptr_t>(x) % 16 != 0 ||
+      (x2 != nullptr && reinterpret_cast<uintptr_t>(x2) % 16 != 0))
+    return FA_ERR_ALIGNMENT;
+  const int es = dtype == FA_DTYPE_BF16 ? 2 : 4;
+  for (const fa_tensor_t* t : {y, y2}) {
+    if (t == nullptr) continue;
+    FA_TRY(check_tensor(t, es, false));
+    if (reinterpret_cast<uintptr_t>(t->data) % 16 != 0 ||
+        (t->stride_b * es) % 16 != 0 || (t->stride_s * es) % 16 != 0 ||
+        (t->stride_h * es) % 16 != 0)
+      return FA_ERR_ALIGNMENT;
+  }
+  FA_TRY(check_sm100());
+  return launch_reduce_cast(dtype, AttnShape{B, S, H, D}, x, x2, n_parts, part_stride, y, y2,
+                            alpha, rope, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int fa_merge_f32(int dtype, int B, int S, int H, int D, const float* o_a, const float* lse_a,
+                 const float* o_b, const float* lse_b, const fa_tensor_t* o, float* lse,
+                 void* stream) {
+  FA_TRY(check_shape(dtype, B, S, H, D));
+  if (D != 128) return FA_ERR_UNSUPPORTED;
+  if (!o_a || !lse_a || !o_b || !lse_b || !lse) return FA_ERR_INVALID_ARG;
+  if (reinterpret_cast<uintptr_t>(o_a) % 16 != 0 || reinterpret_cast<uintptr_t>(o_b) % 16 != 0)
+    return FA_ERR_ALIGNMENT;
+  const int es = dtype == FA_DTYPE_BF16 ? 2 : 4;
+  FA_TRY(check_tensor(o, es, false));
+  if (reinterpret_cast<uintptr_t>(o->data) % 16 != 0 || (o->stride_b * es) % 16 != 0 ||
+      (o->stride_s * es) % 16 != 0 || (o->stride_h * es) % 16 != 0)
+    return FA_ERR_ALIGNMENT;
+  FA_TRY(check_sm100());
+  return launch_merge2(dtype, AttnShape{B, S, H, D}, o_a, lse_a, o_b, lse_b, o, lse,
+                       reinterpret_cast<cudaStream_t>(stream));
 }
 
 int fa_timing_enable(int on) {

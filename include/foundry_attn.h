@@ -230,6 +230,69 @@ int fa_cast_f32(int dtype, int B, int S, int H, int D, const float* x,
                 const fa_rope_t* rope, void* stream);
 
 /*
+ * Peer exchange for sequence parallelism inside one node (one process per
+ * GPU, W <= FA_PEER_MAX ranks). These replace the ring's send/recv with the
+ * GPUs' peer memory; the reference has no multi-GPU path (its op runs on one
+ * device, crates/foundry-spike/src/lib.rs:189-263), so they have no
+ * counterpart there and exist for the sharded long-sequence configuration.
+ *
+ * fa_peer_alloc: a zeroed device allocation of `bytes` on the current device
+ *   and its 64-byte CUDA IPC handle (to be sent to the other ranks).
+ * fa_peer_open: maps another rank's allocation from its handle; fa_peer_close
+ *   unmaps it, fa_peer_free releases an allocation of this rank.
+ * fa_copy_2d: stream-ordered copy of `height` rows of `width` bytes (pitches
+ *   dpitch/spitch) between any two device addresses, peer-mapped ones
+ *   included (the copy engines move the data; no SMs are used).
+ * fa_peer_barrier: every rank tells every other rank that it reached the
+ *   next epoch of `channel` (< FA_PEER_CHANNELS) and waits until all have.
+ *   `flags` holds W pointers to the ranks' flag blocks of
+ *   fa_peer_flags_bytes() bytes each (zeroed at start; this rank's own block
+ *   local, the others peer-mapped). Writes this device issued before the
+ *   barrier on `stream` are visible to the peers once it completes. The wait
+ *   is bounded by timeout_s; expiry sets FA_ERR_DEVICE_TIMEOUT in
+ *   fa_device_status. All ranks must call it the same number of times per
+ *   channel.
+ * fa_bwd_scatter: fa_bwd_partial over kv_len keys whose dK/dV rows are stored
+ *   (fp32, not accumulated) into n_seg separate buffers: key row j goes to
+ *   dk_seg[j / seg], dv_seg[j / seg] at local row j % seg, each buffer fp32
+ *   contiguous (B, seg, H, D). The buffers may be other GPUs' memory (the
+ *   owners of the key rows); the kernel's epilogue stores into them directly.
+ * fa_reduce_cast_f32: y = alpha * inverse_rope(sum_p x[p]) and
+ *   y2 = sum_p x2[p] (y2 may be NULL), p < n_parts, parts part_stride floats
+ *   apart, x and x2 fp32 contiguous (B,S,H,D): the owner's sum of the dK/dV
+ *   contributions it received.
+ * fa_merge_f32: (o, lse) <- the merge of two partial results over disjoint
+ *   key sets, each fp32 normalised o (B,S,H,D) with natural-log lse (B,H,S).
+ */
+#define FA_PEER_MAX 8
+#define FA_PEER_CHANNELS 4
+typedef struct {
+  unsigned char bytes[64];
+} fa_peer_handle_t;
+size_t fa_peer_flags_bytes(void);
+int fa_peer_alloc(size_t bytes, void** ptr, fa_peer_handle_t* handle);
+int fa_peer_open(const fa_peer_handle_t* handle, void** ptr);
+int fa_peer_close(void* ptr);
+int fa_peer_free(void* ptr);
+int fa_copy_2d(void* dst, size_t dpitch, const void* src, size_t spitch,
+               size_t width, size_t height, void* stream);
+int fa_peer_barrier(int rank, int world, void* const* flags, int channel,
+                    double timeout_s, void* stream);
+int fa_bwd_scatter(int dtype, int B, int S, int kv_len, int H, int D,
+                   const fa_tensor_t* q, const fa_tensor_t* k,
+                   const fa_tensor_t* v, const fa_tensor_t* d_o,
+                   const float* lse2_pad, const float* delta_pad, float* dq_acc,
+                   int seg, int n_seg, float* const* dk_seg, float* const* dv_seg,
+                   float scale, void* stream);
+int fa_reduce_cast_f32(int dtype, int B, int S, int H, int D, const float* x,
+                       const float* x2, int n_parts, int64_t part_stride,
+                       const fa_tensor_t* y, const fa_tensor_t* y2, float alpha,
+                       const fa_rope_t* rope, void* stream);
+int fa_merge_f32(int dtype, int B, int S, int H, int D, const float* o_a,
+                 const float* lse_a, const float* o_b, const float* lse_b,
+                 const fa_tensor_t* o, float* lse, void* stream);
+
+/*
  * Backward without a caller workspace. This entry point has no counterpart in
  * the reference. It is for callers that cannot allocate device memory where
  * they call the op: a host framework whose memory pool already owns the GPU
