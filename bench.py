@@ -330,8 +330,9 @@ def main():
     # The timed step replays a CUDA graph of the same public-API calls, so
     # host-side launch overhead (ctypes, descriptor encoding) is not timed as
     # device idle; per-kernel times come from an eager pass with the event hooks.
-    # The ring step holds NCCL exchanges and runs eagerly.
-    if ring_mode:
+    # The NCCL ring step holds NCCL exchanges and runs eagerly; the peer
+    # step (copies, device barriers, kernels on three streams) is captured.
+    if ring_mode and args.transport == "nccl":
         run = step
     else:
         graph = torch.cuda.CUDAGraph()

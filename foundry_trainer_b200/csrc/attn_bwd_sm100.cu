@@ -129,52 +129,75 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src,
       : "memory");
 }
 
-// Writes columns [col0, col0+32) of one dK/dV row held in registers.
+// fp32 output row of key `key` (acc 1-3): the accumulator, or the key's
+// segment buffer (acc 3).
+__device__ __forceinline__ float* f32_row(const Params& p, bool is_dk, int b, int key, int h) {
+  float* base;
+  int64_t row;
+  if (p.acc == 3) {
+    const int o = key / p.seg;
+    base = is_dk ? p.seg_dk[o] : p.seg_dv[o];
+    row = (int64_t)b * p.seg + (key - o * p.seg);
+  } else {
+    base = is_dk ? p.dk_acc : p.dv_acc;
+    row = (int64_t)b * p.kv_len + key;
+  }
+  return base + (row * p.H + h) * 128;
+}
+
+// Writes columns [col0, col0+32) of the 32 fp32 rows a warp holds (lane =
+// row, v = the lane's 32 values) through a 4 KB shared slab: each row goes
+// in as 8 float4 (column c at c ^ (row & 7), no bank conflicts), and comes
+// out as 4 whole rows of 128 contiguous bytes per store instruction, so a
+// segment in another GPU's memory receives full lines over NVLink.
+__device__ __forceinline__ void store_rows32_f32(const Params& p, bool is_dk, int b, int key0,
+                                                 int h, int col0, const float* v,
+                                                 float4* slab, int lane) {
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    slab[lane * 8 + (c ^ (lane & 7))] =
+        make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+  __syncwarp();
+  const int cc = lane & 7;
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    const int rr = it * 4 + (lane >> 3);
+    float4 x = slab[rr * 8 + (cc ^ (rr & 7))];
+    const int key = key0 + rr;
+    if (key < p.kv_len) {
+      float4* dst = reinterpret_cast<float4*>(f32_row(p, is_dk, b, key, h) + col0) + cc;
+      if (p.acc == 1) {
+        const float4 a = *dst;
+        x.x += a.x;
+        x.y += a.y;
+        x.z += a.z;
+        x.w += a.w;
+      }
+      *dst = x;
+    }
+  }
+  __syncwarp();
+}
+
+// Writes columns [col0, col0+32) of one bf16 dK/dV row held in registers.
 __device__ __forceinline__ void store_chunk32(const Params& p, bool is_dk, int b,
                                               int key, int h, int col0,
                                               const float* v) {
-  if (p.acc) {
-    float* base;
-    int64_t row;
-    if (p.acc == 3) {
-      const int o = key / p.seg;
-      base = is_dk ? p.seg_dk[o] : p.seg_dv[o];
-      row = (int64_t)b * p.seg + (key - o * p.seg);
-    } else {
-      base = is_dk ? p.dk_acc : p.dv_acc;
-      row = (int64_t)b * p.kv_len + key;
-    }
-    float* dst = base + (row * p.H + h) * 128 + col0;
-    float4* d4 = reinterpret_cast<float4*>(dst);
+  __nv_bfloat16* dst =
+      (is_dk ? p.dk + (int64_t)b * p.dks_b + (int64_t)key * p.dks_s +
+                   (int64_t)h * p.dks_h
+             : p.dv + (int64_t)b * p.dvs_b + (int64_t)key * p.dvs_s +
+                   (int64_t)h * p.dvs_h) +
+      col0;
+  uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      float4 o = make_float4(v[4 * c + 0], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
-      if (p.acc == 1) {
-        const float4 a = d4[c];
-        o.x += a.x;
-        o.y += a.y;
-        o.z += a.z;
-        o.w += a.w;
-      }
-      d4[c] = o;
-    }
-  } else {
-    __nv_bfloat16* dst =
-        (is_dk ? p.dk + (int64_t)b * p.dks_b + (int64_t)key * p.dks_s +
-                     (int64_t)h * p.dks_h
-               : p.dv + (int64_t)b * p.dvs_b + (int64_t)key * p.dvs_s +
-                     (int64_t)h * p.dvs_h) +
-        col0;
-    uint4* d4 = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      uint4 o;
-      o.x = pack_bf16(v[8 * c + 0], v[8 * c + 1]);
-      o.y = pack_bf16(v[8 * c + 2], v[8 * c + 3]);
-      o.z = pack_bf16(v[8 * c + 4], v[8 * c + 5]);
-      o.w = pack_bf16(v[8 * c + 6], v[8 * c + 7]);
-      d4[c] = o;
-    }
+  for (int c = 0; c < 4; ++c) {
+    uint4 o;
+    o.x = pack_bf16(v[8 * c + 0], v[8 * c + 1]);
+    o.y = pack_bf16(v[8 * c + 2], v[8 * c + 3]);
+    o.z = pack_bf16(v[8 * c + 4], v[8 * c + 5]);
+    o.w = pack_bf16(v[8 * c + 6], v[8 * c + 7]);
+    d4[c] = o;
   }
 }
 
@@ -409,7 +432,9 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
       mbar_arrive(&bars[B_PS]);
     }
     // epilogue: warps 0-3 store dV, warps 10-13 store dK (scaled, and
-    // un-rotated when the op owns the RoPE), one 32-column axis at a time;
+    // un-rotated when the op owns the RoPE), one 32-column axis at a time
+    // (fp32 outputs through per-warp 4 KB slabs of the dS^T tile, free once
+    // the last MMA has completed);
     // the (cos, sin) of the next axis are loaded while this one is stored,
     // the first before the wait for the last MMA
     const bool is_dk = half == 1;
@@ -434,7 +459,12 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
           for (int c = 0; c < 32; ++c) v[c] *= p.scale;
           if (unrot) unrotate_axis(cs, v);
         }
-        if (key < p.kv_len) store_chunk32(p, is_dk, b, key, h, a * 32, v);
+        if (p.acc)
+          store_rows32_f32(p, is_dk, b, kv_tile * kRows + sub * 32, h, a * 32, v,
+                           reinterpret_cast<float4*>(smem + kOffDS + (half * 4 + sub) * 4096),
+                           lane);
+        else if (key < p.kv_len)
+          store_chunk32(p, is_dk, b, key, h, a * 32, v);
         if (unrot && a < 3) {
 #pragma unroll
           for (int u = 0; u < 8; ++u) cs[u] = cs_next[u];

@@ -6,13 +6,14 @@ with the exchange done by the hardware instead of send/recv kernels:
 
   forward   each rank rotates its K shard into a buffer its peers can map
             (CUDA IPC), copies V beside it, and after one barrier the copy
-            engines pull the W-1 remote shards in ring order (r-1, r-2, ...)
-            into a local (B, W*S_loc, H, D) K/V. The block of each shard is
-            folded into one of two fp32 (O, LSE) accumulators as soon as the
-            shard has landed (even steps on the current stream, odd steps on
-            a second one, so two launches of S_loc/256 x H CTAs share the
-            SMs); a final merge writes O and LSE. Copy engines need no SMs, so
-            the pulls run under the attention kernels.
+            engine pulls the W-1 remote shards in ring order (r-1, r-2, ...)
+            into a local
+            (B, W*S_loc, H, D) K/V laid out in that order. The own shard is
+            folded first, then the pulled ones two slots per launch as they
+            land, into two fp32 (O, LSE) accumulators on two streams (so two
+            launches of S_loc/256 x H CTAs share the SMs); a final merge
+            writes O and LSE. Copy engines need no SMs, so the pulls run
+            under the attention kernels.
   backward  the gathered K/V are reused: one `fa_bwd_scatter` launch over all
             W*S_loc keys, whose epilogue stores each key row's fp32 dK/dV
             straight into the receive slot of the rank that owns the row (a
@@ -23,7 +24,11 @@ with the exchange done by the hardware instead of send/recv kernels:
 Two barriers per forward+backward order everything (see `PeerExchange`):
 the forward's (shards published) and the backward's (contributions
 delivered). Buffers peers touch are double-buffered by call parity, so one
-barrier per call is enough for calls that follow one another.
+barrier per call is enough for calls that follow one another. Within one
+forward+backward pair the backward's barrier already orders the next
+forward's writes after every peer's reads (and the forward's barrier the
+next backward's stores after the owner's sum), so a CUDA graph of one pair,
+replayed with its captured parity, is also safe.
 
 The reference runs the op on one device (crates/foundry-spike/src/lib.rs
 :189-263); this path is the long-sequence configuration's multi-GPU form and
@@ -130,6 +135,8 @@ class PeerExchange:
                 self._opened.append(q.value)
         self.bases = bases
         self._flags = (C.c_void_p * self.world)(*[b + self.lay.flags for b in bases])
+        # one copy stream: copies on several streams share one copy engine
+        # and are served stream after stream, not in issue order
         self.copy_stream = torch.cuda.Stream(device=self.device)
         self.side_stream = torch.cuda.Stream(device=self.device)
         self.n_fwd = 0
@@ -157,18 +164,15 @@ class PeerExchange:
                                           self.timeout_s, ops._stream_ptr(stream)),
               "fa_peer_barrier")
 
-    def pull(self, par: int, src: int, k_all: torch.Tensor, v_all: torch.Tensor,
+    def pull(self, par: int, src: int, slot: int, which: int, dst: torch.Tensor,
              stream) -> None:
-        """Copies rank src's published K/V shard into rows [src*S, (src+1)*S)
-        of k_all / v_all ((B, W*S, H, D) contiguous) on `stream`."""
+        """Copies rank src's published K (which 0) or V (1) shard into rows
+        [slot*S, (slot+1)*S) of dst ((B, W*S, H, D) contiguous) on `stream`."""
         B, S, H, D = self.shape
         row = S * H * D * 2
-        lib = _lib.load()
-        for w, dst in ((0, k_all), (1, v_all)):
-            src_ptr = self.bases[src] + self.lay.pub_off(par, w)
-            dst_ptr = dst.data_ptr() + src * row
-            check(lib.fa_copy_2d(dst_ptr, self.world * row, src_ptr, row, row, B,
-                                 ops._stream_ptr(stream)), "fa_copy_2d")
+        src_ptr = self.bases[src] + self.lay.pub_off(par, which)
+        check(_lib.load().fa_copy_2d(dst.data_ptr() + slot * row, self.world * row, src_ptr, row,
+                                     row, B, ops._stream_ptr(stream)), "fa_copy_2d")
 
     def close(self) -> None:
         """Unmaps the peers and frees this rank's buffer (all ranks together)."""
@@ -253,9 +257,23 @@ class PeerKernels:
         return out
 
 
+def fold_groups(world: int) -> List[List[int]]:
+    """Slots of the gathered K/V folded per launch: this rank's own shard
+    alone (it is ready first), then the pulled shards two at a time (two
+    adjacent slots are one contiguous key range)."""
+    groups = [[0]]
+    t = 1
+    while t < world:
+        groups.append(list(range(t, min(t + 2, world))))
+        t += 2
+    return groups
+
+
 def peer_fwd(q, k, v, pos, scale, ex: PeerExchange, kern: PeerKernels):
     """(O, LSE, q_rot, k_all, v_all) of this rank's rows; q/k/v (B, S_loc, H, D)
-    bf16, pos the shard's (S_loc, 4) positions (None: no RoPE)."""
+    bf16, pos the shard's (S_loc, 4) positions (None: no RoPE). k_all / v_all
+    (B, W*S_loc, H, D) hold the rotated K and the V of every shard, slot t
+    (rows [t*S_loc, (t+1)*S_loc)) the shard of rank block_order(rank, W)[t]."""
     B, S, H, D = q.shape
     W, r = ex.world, ex.rank
     dev = q.device
@@ -272,40 +290,44 @@ def peer_fwd(q, k, v, pos, scale, ex: PeerExchange, kern: PeerKernels):
     pub_v.copy_(v)
     k_all = torch.empty((B, W * S, H, D), device=dev, dtype=q.dtype)
     v_all = torch.empty_like(k_all)
+    # this rank's own shard into slot 0 while every SM is still free
+    k_all[:, :S].copy_(pub_k)
+    v_all[:, :S].copy_(pub_v)
     o = torch.empty((B, S, H, D), device=dev, dtype=q.dtype)
     lse = torch.empty((B, H, S), device=dev, dtype=torch.float32)
-    if W > 1:
-        ex.barrier(0)  # every rank's shard is published
-    # copy engines: the remote shards in fold order, then this rank's own
+    if W == 1:
+        kern.fwd_fold(q_r, pub_k, pub_v, scale, o, lse, 0, True, o, lse)
+        return o, lse, q_r, k_all, v_all
+    ex.barrier(0)  # every rank's shard is published
+    # copy engine: the remote shards in fold order
     order = block_order(r, W)
     cs = ex.copy_stream
     cs.wait_stream(cur)
-    landed = []
-    for src in order[1:] + order[:1]:
-        ex.pull(par, src, k_all, v_all, cs)
-        ev = torch.cuda.Event()
-        ev.record(cs)
-        landed.append(ev)
-    landed = landed[-1:] + landed[:-1]  # landed[t] <-> order[t]
-    if W == 1:
-        kern.fwd_fold(q_r, pub_k, pub_v, scale, o, lse, 0, True, o, lse)
-    else:
-        acc = [(torch.empty((B, S, H, D), device=dev, dtype=torch.float32),
-                torch.empty((B, H, S), device=dev, dtype=torch.float32)) for _ in range(2)]
-        side = ex.side_stream
-        side.wait_stream(cur)
-        for t, src in enumerate(order):
-            st = cur if t % 2 == 0 else side
-            if t == 0:
-                kb, vb = pub_k, pub_v
-            else:
+    landed = [None] * W
+    for t in range(1, W):
+        ex.pull(par, order[t], t, 0, k_all, cs)
+        ex.pull(par, order[t], t, 1, v_all, cs)
+        landed[t] = torch.cuda.Event()
+        landed[t].record(cs)
+    # two fp32 (O, LSE) accumulators folded on two streams, then merged
+    acc = [(torch.empty((B, S, H, D), device=dev, dtype=torch.float32),
+            torch.empty((B, H, S), device=dev, dtype=torch.float32)) for _ in range(2)]
+    side = ex.side_stream
+    side.wait_stream(cur)
+    steps = [0, 0]
+    for g, slots in enumerate(fold_groups(W)):
+        a = g % 2
+        st = cur if a == 0 else side
+        for t in slots:
+            if landed[t] is not None:
                 st.wait_event(landed[t])
-                kb, vb = k_all[:, src * S:(src + 1) * S], v_all[:, src * S:(src + 1) * S]
-            o_acc, lse_acc = acc[t % 2]
-            kern.fwd_fold(q_r, kb, vb, scale, o_acc, lse_acc, t // 2, False, o, lse, stream=st)
-        cur.wait_stream(side)
-        kern.merge(acc[0][0], acc[0][1], acc[1][0], acc[1][1], o, lse)
-    cur.wait_event(landed[0])  # this rank's own slot of k_all / v_all
+        lo, hi = slots[0] * S, (slots[-1] + 1) * S
+        kb, vb = (pub_k, pub_v) if slots == [0] else (k_all[:, lo:hi], v_all[:, lo:hi])
+        kern.fwd_fold(q_r, kb, vb, scale, acc[a][0], acc[a][1], steps[a], False, o, lse,
+                      stream=st)
+        steps[a] += 1
+    cur.wait_stream(side)
+    kern.merge(acc[0][0], acc[0][1], acc[1][0], acc[1][1], o, lse)
     return o, lse, q_r, k_all, v_all
 
 
@@ -321,8 +343,11 @@ def peer_bwd(q_r, k_all, v_all, o, d_o, lse, pos, scale, ex: PeerExchange, kern:
     delta_pad = torch.empty((B, H, sp), device=dev, dtype=torch.float32)
     kern.bwd_prepare(o, d_o, lse, lse2_pad, delta_pad)
     dq_acc = torch.zeros((B, H, sp, D), device=dev, dtype=torch.float32)
+    # key slot t of k_all belongs to rank block_order(rank, W)[t]
+    order = block_order(ex.rank, W)
+    dk_ptrs, dv_ptrs = ex.recv_ptrs(par, 0), ex.recv_ptrs(par, 1)
     kern.bwd_scatter(q_r, k_all, v_all, d_o, lse2_pad, delta_pad, dq_acc, S,
-                     ex.recv_ptrs(par, 0), ex.recv_ptrs(par, 1), scale)
+                     [dk_ptrs[o] for o in order], [dv_ptrs[o] for o in order], scale)
     if W > 1:
         ex.barrier(1)  # every rank's contribution to this rank's keys has landed
     dq = torch.empty((B, S, H, D), device=dev, dtype=q_r.dtype)

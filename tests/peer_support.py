@@ -62,16 +62,14 @@ class ThreadPeers:
                 torch.cuda.synchronize()
                 peers.barrier_.wait()
 
-            def pull(self, par, src, k_all, v_all, stream):
+            def pull(self, par, src, slot, which, dst, stream):
                 from foundry_trainer_b200 import _lib, ops
                 B, S, H, D = peers.shape
                 row = S * H * D * 2
-                lib = _lib.load()
-                for w, dst in ((0, k_all), (1, v_all)):
-                    src_ptr = peers.pub[src][par][w].data_ptr()
-                    rc = lib.fa_copy_2d(dst.data_ptr() + src * row, peers.world * row, src_ptr,
-                                        row, row, B, ops._stream_ptr(stream))
-                    assert rc == 0, rc
+                src_ptr = peers.pub[src][par][which].data_ptr()
+                rc = _lib.load().fa_copy_2d(dst.data_ptr() + slot * row, peers.world * row,
+                                            src_ptr, row, row, B, ops._stream_ptr(stream))
+                assert rc == 0, rc
 
         return _Exchange()
 

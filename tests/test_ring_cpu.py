@@ -65,3 +65,33 @@ def test_ring_matches_single_sequence_oracle(world, S):
         assert calls.count("fwd_partial") == world
         assert calls.count("bwd_partial") == world
         assert calls.count("add") == world - 1
+
+
+def test_peer_schedule_covers_every_shard_once():
+    from foundry_trainer_b200 import peer
+    for world in range(1, 9):
+        for rank in range(world):
+            order = peer.block_order(rank, world)
+            assert order[0] == rank and sorted(order) == list(range(world))
+        groups = peer.fold_groups(world)
+        assert groups[0] == [0]
+        assert [t for g in groups for t in g] == list(range(world))
+        assert all(len(g) <= 2 and g == list(range(g[0], g[-1] + 1)) for g in groups)
+
+
+def test_peer_layout_regions_are_disjoint_and_aligned():
+    from foundry_trainer_b200 import peer
+    for world in (1, 2, 8):
+        lay = peer.Layout(1, 2112, 24, 128, world, 256)
+        spans = [(0, 256)]
+        for par in range(2):
+            for w in range(2):
+                spans.append((lay.pub_off(par, w), lay.pub_off(par, w) + lay.n * 2))
+            for src in range(world):
+                for w in range(2):
+                    o = lay.recv_off(par, src, w)
+                    spans.append((o, o + lay.n * 4))
+        spans.sort()
+        assert all(a[1] <= b[0] for a, b in zip(spans, spans[1:]))
+        assert spans[-1][1] <= lay.total
+        assert all(a % 16 == 0 for a, _ in spans)
