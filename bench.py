@@ -201,6 +201,9 @@ def main():
     ap.add_argument("--transport", default="peer", choices=["peer", "nccl"],
                     help="c5 exchange: peer memory (copy-engine pulls, peer stores, device "
                          "barriers) or NCCL send/recv round a ring")
+    ap.add_argument("--peer-copy", default="ce", choices=["ce", "sm"],
+                    help="peer transport: K/V pulled by the copy engines (ce) or by a copy "
+                         "kernel beside the attention CTAs (sm)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--ncu-case", action="store_true",
@@ -251,7 +254,8 @@ def main():
         scale = ops.default_scale(cfg.D)
         if args.transport == "peer":
             from foundry_trainer_b200 import peer
-            ex, pkern = peer.PeerExchange(cfg.B, n_loc, cfg.H, cfg.D), peer.PeerKernels()
+            ex = peer.PeerExchange(cfg.B, n_loc, cfg.H, cfg.D, copy=args.peer_copy)
+            pkern = peer.PeerKernels()
 
             def make_step(q, k, v, d_o):
                 outs = {}
@@ -517,13 +521,17 @@ def main():
     if rank != 0:
         return
     if ring_mode and args.transport == "peer":
-        # fwd: rope q, rope k, W folds (+ merge and barrier when W > 1);
-        # bwd: prepare, one scatter launch, reduce-cast, dQ cast (+ barrier)
-        launches_per_step = 2 + world + 4 + (3 if world > 1 else 0)
+        # fwd: rope q, rope k, the fold launches (+ merge and barrier, and
+        # with the copy kernel 2 per pulled shard, when W > 1); bwd: prepare,
+        # one scatter launch, reduce-cast, dQ cast (+ barrier)
+        n_folds = len(peer.fold_groups(world))
+        launches_per_step = (2 + n_folds + 4 + (3 if world > 1 else 0) +
+                             (2 * (world - 1) if args.peer_copy == "sm" else 0))
         workload = (f"{cfg.name}: B={cfg.B} H={cfg.H} S={cfg.S} ({cfg.txt} text + "
                     f"{cfg.grid}x{cfg.grid} image) D={cfg.D}, one sequence sharded "
                     f"{n_loc} rows per rank, non-causal, axial RoPE")
-        parallelism = (f"sequence-parallel x{world} over peer memory (copy-engine K/V pulls, "
+        parallelism = (f"sequence-parallel x{world} over peer memory (K/V pulled by "
+                       f"{'a copy kernel' if args.peer_copy == 'sm' else 'the copy engines'}, "
                        f"dK/dV rows stored into the owners by the backward's epilogue)")
     elif ring_mode:
         # fwd: rope q, rope k, W blocks + W merges, O cast; bwd: prepare,

@@ -95,6 +95,8 @@ SIGNATURES = {
     "fa_peer_free": (C.c_int, [C.c_void_p]),
     "fa_copy_2d": (C.c_int, [C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t, C.c_size_t,
                              C.c_size_t, C.c_void_p]),
+    "fa_copy_2d_sm": (C.c_int, [C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t, C.c_size_t,
+                                C.c_size_t, C.c_int, C.c_void_p]),
     "fa_peer_barrier": (C.c_int, [C.c_int, C.c_int, C.POINTER(C.c_void_p), C.c_int, C.c_double,
                                   C.c_void_p]),
     "fa_bwd_scatter": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _T, _T, _T,

@@ -132,6 +132,8 @@ int launch_qk_norm_rope_bwd(int B, int T, int I, int H, const fa_tensor_t* x_txt
 // scaled by alpha), and the merge of two fp32 (O, LSE) partials
 int launch_peer_barrier(int rank, int world, void* const* flags, int channel,
                         double timeout_s, cudaStream_t stream);
+int launch_copy2d_sm(void* dst, size_t dpitch, const void* src, size_t spitch, size_t width,
+                     size_t height, int ctas, cudaStream_t stream);
 int launch_reduce_cast(int dtype, const AttnShape& sh, const float* x, const float* x2,
                        int n_parts, int64_t part_stride, const fa_tensor_t* y,
                        const fa_tensor_t* y2, float alpha, const fa_rope_t* rope,

@@ -694,6 +694,20 @@ int fa_copy_2d(void* dst, size_t dpitch, const void* src, size_t spitch, size_t 
   return record_cuda_error(e);
 }
 
+int fa_copy_2d_sm(void* dst, size_t dpitch, const void* src, size_t spitch, size_t width,
+                  size_t height, int ctas, void* stream) {
+  if (width == 0 || height == 0) return FA_OK;
+  if (dst == nullptr || src == nullptr || dpitch < width || spitch < width || ctas < 1)
+    return FA_ERR_INVALID_ARG;
+  if (width % 16 != 0 || dpitch % 16 != 0 || spitch % 16 != 0 ||
+      reinterpret_cast<uintptr_t>(dst) % 16 != 0 || reinterpret_cast<uintptr_t>(src) % 16 != 0)
+    return FA_ERR_ALIGNMENT;
+  if (height > 65535) return FA_ERR_TOO_LARGE;  // one grid row per copied row
+  FA_TRY(check_sm100());
+  return launch_copy2d_sm(dst, dpitch, src, spitch, width, height, ctas,
+                          reinterpret_cast<cudaStream_t>(stream));
+}
+
 int fa_peer_barrier(int rank, int world, void* const* flags, int channel, double timeout_s,
                     void* stream) {
   if (world < 1 || world > FA_PEER_MAX || rank < 0 || rank >= world || flags == nullptr ||

@@ -8,9 +8,9 @@
 // NVSwitch, so the exchange is done with the hardware directly:
 //   * buffers that peers read or write are plain device allocations shared
 //     through CUDA IPC handles (no multicast object is created);
-//   * K/V shards are pulled by the copy engines (cudaMemcpy2DAsync from a
-//     peer's buffer), which run beside the attention kernels without taking
-//     SMs from them;
+//   * K/V shards are pulled from a peer's buffer by the copy engines
+//     (cudaMemcpy2DAsync) or by a copy kernel whose small CTAs fit beside the
+//     attention CTAs; either runs under the attention kernels;
 //   * the backward kernel's epilogue stores each dK/dV row straight into the
 //     owner rank's receive slot (attn_bwd_sm100.cu, scatter mode);
 //   * ranks order these steps with a small barrier kernel over flags in the
@@ -19,6 +19,8 @@
 // This file also holds the two reductions of that path: the sum of the W
 // dK/dV contributions an owner receives (with the inverse RoPE and the cast
 // to bf16) and the merge of two fp32 (O, LSE) partial accumulators.
+#include <algorithm>
+
 #include "attn_common.h"
 #include "rope.cuh"
 #include "sm100_ptx.cuh"
@@ -183,7 +185,40 @@ merge2_kernel(const float* o_a, const float* lse_a, const float* o_b, const floa
   if (lane == 0) lse[li] = mx + logf(ea + eb);
 }
 
+// One row (blockIdx.y) of width 16-byte units per grid row, copied by SMs
+// with 16-byte loads and stores, 4 in flight per thread. Four warps, at most
+// 40 registers and no shared memory: a CTA fits beside one attention CTA on
+// an SM (which leaves ~6400 registers and ~1.8 KB of shared memory), so the
+// copy runs under the forward's folds. Sources may be peers' memory.
+constexpr int kCopyThreads = 128;
+constexpr int kCopyUnroll = 4;
+__global__ void __launch_bounds__(kCopyThreads, 12)
+copy_rows_kernel(uint8_t* dst, int64_t dpitch, const uint8_t* src, int64_t spitch, int64_t w16) {
+  const uint4* s = reinterpret_cast<const uint4*>(src + (int64_t)blockIdx.y * spitch);
+  uint4* d = reinterpret_cast<uint4*>(dst + (int64_t)blockIdx.y * dpitch);
+  const int64_t stride = (int64_t)gridDim.x * kCopyThreads;
+  int64_t i = (int64_t)blockIdx.x * kCopyThreads + threadIdx.x;
+  for (; i + (kCopyUnroll - 1) * stride < w16; i += kCopyUnroll * stride) {
+    uint4 v[kCopyUnroll];
+#pragma unroll
+    for (int u = 0; u < kCopyUnroll; ++u) v[u] = __ldcs(s + i + u * stride);
+#pragma unroll
+    for (int u = 0; u < kCopyUnroll; ++u) d[i + u * stride] = v[u];
+  }
+  for (; i < w16; i += stride) d[i] = __ldcs(s + i);
+}
+
 }  // namespace peer
+
+int launch_copy2d_sm(void* dst, size_t dpitch, const void* src, size_t spitch, size_t width,
+                     size_t height, int ctas, cudaStream_t stream) {
+  const int64_t w16 = (int64_t)(width / 16);
+  const int per_row = std::max(1, ctas / (int)std::min<size_t>(height, (size_t)ctas));
+  peer::copy_rows_kernel<<<dim3(per_row, (unsigned)height), peer::kCopyThreads, 0, stream>>>(
+      reinterpret_cast<uint8_t*>(dst), (int64_t)dpitch, reinterpret_cast<const uint8_t*>(src),
+      (int64_t)spitch, w16);
+  return launch_status();
+}
 
 int launch_peer_barrier(int rank, int world, void* const* flags, int channel,
                         double timeout_s, cudaStream_t stream) {

@@ -46,6 +46,7 @@ from . import _lib, ops
 from ._lib import check
 
 _ALIGN = 4096
+_SM_COPY_CTAS = 148  # one small copy CTA per SM of a B200
 
 
 def _align(x: int) -> int:
@@ -102,13 +103,16 @@ class PeerExchange:
     construct it together (the IPC handles are exchanged over the group)."""
 
     def __init__(self, B: int, S: int, H: int, D: int, *, group=None, timeout_s: float = 30.0,
-                 device: Optional[torch.device] = None):
+                 device: Optional[torch.device] = None, copy: str = "ce"):
         self.group = group
         dist_on = dist.is_initialized()
         self.world = dist.get_world_size(group) if dist_on else 1
         self.rank = dist.get_rank(group) if dist_on else 0
         if self.world > 8:
             raise ValueError("the peer exchange spans at most 8 ranks (one node)")
+        if copy not in ("ce", "sm"):
+            raise ValueError("copy must be 'ce' (copy engines) or 'sm' (a copy kernel)")
+        self.copy = copy
         self.shape = (B, S, H, D)
         self.device = device if device is not None else torch.device("cuda",
                                                                      torch.cuda.current_device())
@@ -171,8 +175,14 @@ class PeerExchange:
         B, S, H, D = self.shape
         row = S * H * D * 2
         src_ptr = self.bases[src] + self.lay.pub_off(par, which)
-        check(_lib.load().fa_copy_2d(dst.data_ptr() + slot * row, self.world * row, src_ptr, row,
-                                     row, B, ops._stream_ptr(stream)), "fa_copy_2d")
+        lib = _lib.load()
+        if self.copy == "sm":
+            check(lib.fa_copy_2d_sm(dst.data_ptr() + slot * row, self.world * row, src_ptr, row,
+                                    row, B, _SM_COPY_CTAS, ops._stream_ptr(stream)),
+                  "fa_copy_2d_sm")
+        else:
+            check(lib.fa_copy_2d(dst.data_ptr() + slot * row, self.world * row, src_ptr, row,
+                                 row, B, ops._stream_ptr(stream)), "fa_copy_2d")
 
     def close(self) -> None:
         """Unmaps the peers and frees this rank's buffer (all ranks together)."""
@@ -269,11 +279,21 @@ def fold_groups(world: int) -> List[List[int]]:
     return groups
 
 
-def peer_fwd(q, k, v, pos, scale, ex: PeerExchange, kern: PeerKernels):
+def _mark(trace: Optional[list], name: str, stream=None) -> None:
+    """Appends (name, timing event recorded on `stream`) when tracing."""
+    if trace is not None:
+        e = torch.cuda.Event(enable_timing=True)
+        e.record(stream if stream is not None else torch.cuda.current_stream())
+        trace.append((name, e))
+
+
+def peer_fwd(q, k, v, pos, scale, ex: PeerExchange, kern: PeerKernels,
+             trace: Optional[list] = None):
     """(O, LSE, q_rot, k_all, v_all) of this rank's rows; q/k/v (B, S_loc, H, D)
     bf16, pos the shard's (S_loc, 4) positions (None: no RoPE). k_all / v_all
     (B, W*S_loc, H, D) hold the rotated K and the V of every shard, slot t
-    (rows [t*S_loc, (t+1)*S_loc)) the shard of rank block_order(rank, W)[t]."""
+    (rows [t*S_loc, (t+1)*S_loc)) the shard of rank block_order(rank, W)[t].
+    `trace` (a list) collects device events at the schedule's milestones."""
     B, S, H, D = q.shape
     W, r = ex.world, ex.rank
     dev = q.device
@@ -281,6 +301,7 @@ def peer_fwd(q, k, v, pos, scale, ex: PeerExchange, kern: PeerKernels):
     par = ex.n_fwd % 2
     ex.n_fwd += 1
     pub_k, pub_v = ex.pub(par)
+    _mark(trace, "start")
     if pos is not None:
         q_r = kern.rope(q, pos)
         kern.rope(k, pos, out=pub_k)
@@ -295,10 +316,13 @@ def peer_fwd(q, k, v, pos, scale, ex: PeerExchange, kern: PeerKernels):
     v_all[:, :S].copy_(pub_v)
     o = torch.empty((B, S, H, D), device=dev, dtype=q.dtype)
     lse = torch.empty((B, H, S), device=dev, dtype=torch.float32)
+    _mark(trace, "rope+pub")
     if W == 1:
         kern.fwd_fold(q_r, pub_k, pub_v, scale, o, lse, 0, True, o, lse)
+        _mark(trace, "fold0.end")
         return o, lse, q_r, k_all, v_all
     ex.barrier(0)  # every rank's shard is published
+    _mark(trace, "barrier0")
     # copy engine: the remote shards in fold order
     order = block_order(r, W)
     cs = ex.copy_stream
@@ -309,6 +333,7 @@ def peer_fwd(q, k, v, pos, scale, ex: PeerExchange, kern: PeerKernels):
         ex.pull(par, order[t], t, 1, v_all, cs)
         landed[t] = torch.cuda.Event()
         landed[t].record(cs)
+        _mark(trace, f"pull{t}", cs)
     # two fp32 (O, LSE) accumulators folded on two streams, then merged
     acc = [(torch.empty((B, S, H, D), device=dev, dtype=torch.float32),
             torch.empty((B, H, S), device=dev, dtype=torch.float32)) for _ in range(2)]
@@ -323,15 +348,19 @@ def peer_fwd(q, k, v, pos, scale, ex: PeerExchange, kern: PeerKernels):
                 st.wait_event(landed[t])
         lo, hi = slots[0] * S, (slots[-1] + 1) * S
         kb, vb = (pub_k, pub_v) if slots == [0] else (k_all[:, lo:hi], v_all[:, lo:hi])
+        _mark(trace, f"fold{g}.begin", st)
         kern.fwd_fold(q_r, kb, vb, scale, acc[a][0], acc[a][1], steps[a], False, o, lse,
                       stream=st)
+        _mark(trace, f"fold{g}.end", st)
         steps[a] += 1
     cur.wait_stream(side)
     kern.merge(acc[0][0], acc[0][1], acc[1][0], acc[1][1], o, lse)
+    _mark(trace, "merge")
     return o, lse, q_r, k_all, v_all
 
 
-def peer_bwd(q_r, k_all, v_all, o, d_o, lse, pos, scale, ex: PeerExchange, kern: PeerKernels):
+def peer_bwd(q_r, k_all, v_all, o, d_o, lse, pos, scale, ex: PeerExchange, kern: PeerKernels,
+             trace: Optional[list] = None):
     """(dq, dk, dv) of this rank's rows w.r.t. the pre-rotation q/k."""
     B, S, H, D = q_r.shape
     W = ex.world
@@ -343,18 +372,23 @@ def peer_bwd(q_r, k_all, v_all, o, d_o, lse, pos, scale, ex: PeerExchange, kern:
     delta_pad = torch.empty((B, H, sp), device=dev, dtype=torch.float32)
     kern.bwd_prepare(o, d_o, lse, lse2_pad, delta_pad)
     dq_acc = torch.zeros((B, H, sp, D), device=dev, dtype=torch.float32)
+    _mark(trace, "prepare")
     # key slot t of k_all belongs to rank block_order(rank, W)[t]
     order = block_order(ex.rank, W)
     dk_ptrs, dv_ptrs = ex.recv_ptrs(par, 0), ex.recv_ptrs(par, 1)
     kern.bwd_scatter(q_r, k_all, v_all, d_o, lse2_pad, delta_pad, dq_acc, S,
                      [dk_ptrs[o] for o in order], [dv_ptrs[o] for o in order], scale)
+    _mark(trace, "scatter")
     if W > 1:
         ex.barrier(1)  # every rank's contribution to this rank's keys has landed
+    _mark(trace, "barrier1")
     dq = torch.empty((B, S, H, D), device=dev, dtype=q_r.dtype)
     dk = torch.empty_like(dq)
     dv = torch.empty_like(dq)
     kern.reduce_cast(ex.recv(par), pos, dk, dv)
+    _mark(trace, "reduce")
     kern.cast(dq_acc, 1, scale, pos, dq)
+    _mark(trace, "dqcast")
     return dq, dk, dv
 
 

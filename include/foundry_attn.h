@@ -243,6 +243,9 @@ int fa_cast_f32(int dtype, int B, int S, int H, int D, const float* x,
  * fa_copy_2d: stream-ordered copy of `height` rows of `width` bytes (pitches
  *   dpitch/spitch) between any two device addresses, peer-mapped ones
  *   included (the copy engines move the data; no SMs are used).
+ * fa_copy_2d_sm: the same copy done by `ctas` small CTAs of SMs (16-byte
+ *   loads and stores; width, pitches and addresses 16-byte aligned). Each CTA
+ *   fits beside one attention CTA on an SM, so it runs under the kernels.
  * fa_peer_barrier: every rank tells every other rank that it reached the
  *   next epoch of `channel` (< FA_PEER_CHANNELS) and waits until all have.
  *   `flags` holds W pointers to the ranks' flag blocks of
@@ -276,6 +279,8 @@ int fa_peer_close(void* ptr);
 int fa_peer_free(void* ptr);
 int fa_copy_2d(void* dst, size_t dpitch, const void* src, size_t spitch,
                size_t width, size_t height, void* stream);
+int fa_copy_2d_sm(void* dst, size_t dpitch, const void* src, size_t spitch,
+                  size_t width, size_t height, int ctas, void* stream);
 int fa_peer_barrier(int rank, int world, void* const* flags, int channel,
                     double timeout_s, void* stream);
 int fa_bwd_scatter(int dtype, int B, int S, int kv_len, int H, int D,

@@ -25,8 +25,9 @@ import torch
 
 
 class ThreadPeers:
-    def __init__(self, world: int, shape, device="cuda"):
+    def __init__(self, world: int, shape, device="cuda", copy="ce"):
         self.world = world
+        self.copy = copy
         self.shape = tuple(shape)
         self.barrier_ = threading.Barrier(world, timeout=120)
         B, S, H, D = self.shape
@@ -67,14 +68,18 @@ class ThreadPeers:
                 B, S, H, D = peers.shape
                 row = S * H * D * 2
                 src_ptr = peers.pub[src][par][which].data_ptr()
-                rc = _lib.load().fa_copy_2d(dst.data_ptr() + slot * row, peers.world * row,
-                                            src_ptr, row, row, B, ops._stream_ptr(stream))
+                lib = _lib.load()
+                args = (dst.data_ptr() + slot * row, peers.world * row, src_ptr, row, row, B)
+                if peers.copy == "sm":
+                    rc = lib.fa_copy_2d_sm(*args, 148, ops._stream_ptr(stream))
+                else:
+                    rc = lib.fa_copy_2d(*args, ops._stream_ptr(stream))
                 assert rc == 0, rc
 
         return _Exchange()
 
 
-def peer_rank(rank, world, port, arrays, results, steps=1):
+def peer_rank(rank, world, port, arrays, results, steps=1, copy="ce"):
     """One process per GPU: peer_attention of its shard, `steps` times (the
     results of the last step are reported)."""
     import torch.distributed as dist
@@ -93,7 +98,7 @@ def peer_rank(rank, world, port, arrays, results, steps=1):
         n = q.shape[1] // world
         sl = slice(rank * n, (rank + 1) * n)
         B, _, H, D = q.shape
-        ex = peer.PeerExchange(B, n, H, D)
+        ex = peer.PeerExchange(B, n, H, D, copy=copy)
         for _ in range(steps):
             to = lambda t: t[:, sl].to(torch.bfloat16).cuda().requires_grad_(True)
             qs, ks, vs = to(q), to(k), to(v)

@@ -183,11 +183,12 @@ def test_peer_single_rank_autograd():
     _check([(f(o), f(qs.grad), f(ks.grad), f(vs.grad))], _oracle(q, k, v, d_o, pos), "autograd")
 
 
-@pytest.mark.parametrize("world,S", [(2, 512), (3, 900), (4, 1056), (8, 1024)])
-def test_peer_thread_emulated_ranks_match_oracle(world, S):
+@pytest.mark.parametrize("world,S,copy", [(2, 512, "ce"), (3, 900, "ce"), (4, 1056, "ce"),
+                                          (8, 1024, "ce"), (4, 1056, "sm")])
+def test_peer_thread_emulated_ranks_match_oracle(world, S, copy):
     from foundry_trainer_b200 import ops
     q, k, v, d_o, pos = _problem(S, 2, seed=30 + world)
-    peers = peer_support.ThreadPeers(world, (1, S // world, 2, 128))
+    peers = peer_support.ThreadPeers(world, (1, S // world, 2, 128), copy=copy)
     outs, errors = [None] * world, []
 
     def body(r):
@@ -215,15 +216,28 @@ def _free_port():
         return s.getsockname()[1]
 
 
+def test_copy_rows_kernel_matches_strided_copy():
+    from foundry_trainer_b200 import _lib, ops
+    src = torch.randint(0, 255, (3, 5000 * 16), dtype=torch.uint8, device="cuda")
+    dst = torch.zeros((3, 7000 * 16), dtype=torch.uint8, device="cuda")
+    rc = _lib.load().fa_copy_2d_sm(dst.data_ptr() + 512, dst.stride(0), src.data_ptr(),
+                                   src.stride(0), 4992 * 16, 3, 37, ops._stream_ptr(None))
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert torch.equal(dst[:, 512:512 + 4992 * 16], src[:, :4992 * 16])
+    assert int(dst[:, :512].sum()) == 0 and int(dst[:, 512 + 4992 * 16:].sum()) == 0
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_peer_two_gpu_ranks_match_oracle():
+@pytest.mark.parametrize("copy", ["ce", "sm"])
+def test_peer_two_gpu_ranks_match_oracle(copy):
     q, k, v, d_o, pos = _problem(2 * 1056, 3, seed=5)
     ctx = mp.get_context("spawn")
     results = ctx.Queue()
     arrays = tuple(t.numpy() for t in (q, k, v, d_o, pos))
     port = _free_port()
-    procs = [ctx.Process(target=peer_support.peer_rank, args=(r, 2, port, arrays, results, 3))
-             for r in range(2)]
+    procs = [ctx.Process(target=peer_support.peer_rank,
+                         args=(r, 2, port, arrays, results, 3, copy)) for r in range(2)]
     for p in procs:
         p.start()
     got = {}
@@ -238,4 +252,4 @@ def test_peer_two_gpu_ranks_match_oracle():
                 p.kill()
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     assert all(got[r][4] == 0 for r in range(2))
-    _check([got[r][:4] for r in range(2)], _oracle(q, k, v, d_o, pos), "peer w2")
+    _check([got[r][:4] for r in range(2)], _oracle(q, k, v, d_o, pos), f"peer w2 {copy}")
