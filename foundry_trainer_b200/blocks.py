@@ -1,0 +1,346 @@
+"""The callers of the attention op: the double- and single-stream DiT blocks
+with LoRA, and the AdamW step on the LoRA factors.
+
+Restates the reference's block code (crates/foundry-spike/src/lib.rs) over a
+weight dictionary keyed like its fixtures and its `Weights` map
+("weights/<name>.weight", ".bias", ".lora_a", ".lora_b"):
+
+  linear            lib.rs:270-287  y = x W^T [+ b] + s * (x A^T) B^T
+  swiglu            lib.rs:291-295  down(silu(gate(x)) * up(x))
+  layer_norm_mod    lib.rs:60-71    LayerNorm in fp32, (1 + scale) * n + shift, cast
+  double_block      lib.rs:301-392
+  single_block      lib.rs:394-456
+  mse               lib.rs:458-463
+  AdamW             lib.rs:472-505  fp32 moments, bias-corrected, weight decay 0
+
+The attention of each block is a callable (`attention=`): by default the
+B200 op with its fused q/k RMSNorm + RoPE prologue (`attn.JointAttention`
+for the double block, `SingleAttention` here for the single block), which
+take the per-stream projections before the norm and return the attention
+output. Everything else (the linears, norms, modulation, MLPs) is torch on
+the device: cuBLAS GEMMs and elementwise kernels.
+
+Two block variants share this code:
+  * the reference's (its fixtures and klein harness): one modulation linear
+    for both streams of the double block (`<prefix>.mod`) or one per stream
+    (`<prefix>.img.mod`, `<prefix>.txt.mod`, bin/throughput.rs:480-572),
+    SwiGLU MLPs, optional biases;
+  * the FLUX-style block of the LoRA benchmark configuration: modulation per
+    stream, a 4x GELU (tanh) MLP `<prefix>.<stream>.mlp.fc1/.fc2`, LoRA on
+    q/k/v/out of both streams (`make_c3_weights`).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Callable, Dict, List, Optional, Tuple
+
+import torch
+import torch.nn.functional as F
+
+from . import attn, ops
+
+Weights = Dict[str, torch.Tensor]
+
+NORM_EPS = 1e-6  # lib.rs:26
+
+
+def _get(w: Weights, key: str) -> torch.Tensor:
+    t = w.get(key)
+    if t is None:
+        raise KeyError(f"weight missing: {key}")
+    return t
+
+
+# ------------------------------------------------------------------ ops
+
+def linear(w: Weights, name: str, x: torch.Tensor, lora_scale: float) -> torch.Tensor:
+    """x W^T (+ b) (+ lora_scale * (x A^T) B^T when the LoRA factors exist)."""
+    y = F.linear(x, _get(w, f"weights/{name}.weight"))
+    b = w.get(f"weights/{name}.bias")
+    if b is not None:
+        y = y + b
+    a, bb = w.get(f"weights/{name}.lora_a"), w.get(f"weights/{name}.lora_b")
+    if a is not None and bb is not None:
+        y = y + F.linear(F.linear(x, a), bb) * lora_scale
+    return y
+
+
+def swiglu(w: Weights, name: str, x: torch.Tensor, lora_scale: float) -> torch.Tensor:
+    gate = F.silu(linear(w, f"{name}.gate", x, lora_scale))
+    up = linear(w, f"{name}.up", x, lora_scale)
+    return linear(w, f"{name}.down", gate * up, lora_scale)
+
+
+def gelu_mlp(w: Weights, name: str, x: torch.Tensor, lora_scale: float) -> torch.Tensor:
+    """The FLUX MLP: fc2(gelu_tanh(fc1(x))), hidden 4x."""
+    return linear(w, f"{name}.fc2", F.gelu(linear(w, f"{name}.fc1", x, lora_scale),
+                                           approximate="tanh"), lora_scale)
+
+
+def layer_norm_mod(x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor,
+                   eps: float = NORM_EPS) -> torch.Tensor:
+    xf = x.float()
+    mean = xf.mean(dim=-1, keepdim=True)
+    c = xf - mean
+    var = (c * c).mean(dim=-1, keepdim=True)
+    n = c / torch.sqrt(var + eps)
+    return (n * (scale.float() + 1.0) + shift.float()).to(x.dtype)
+
+
+def mse(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    d = a.float() - b.float()
+    return (d * d).mean()
+
+
+def _mlp(w: Weights, name: str, x: torch.Tensor, lora_scale: float) -> torch.Tensor:
+    if f"weights/{name}.fc1.weight" in w:
+        return gelu_mlp(w, name, x, lora_scale)
+    return swiglu(w, name, x, lora_scale)
+
+
+def _modulation(w: Weights, name: str, temb: torch.Tensor, dim: int,
+                lora_scale: float) -> List[torch.Tensor]:
+    """The six (dim,) chunks of linear(silu(temb)): shift1, scale1, gate1,
+    shift2, scale2, gate2 (the reference feeds silu(temb), lib.rs:310-317)."""
+    out = linear(w, name, F.silu(temb).reshape(1, dim), lora_scale).reshape(6 * dim)
+    return list(out.split(dim))
+
+
+# ------------------------------------------------------ attention callables
+
+class SingleAttention:
+    """Attention of the single-stream block (lib.rs:415-446) on the B200 op:
+    q/k RMSNorm with their weights and RoPE at `positions` in one fused pass
+    each (fa_qk_norm_rope_fwd with no text stream), the op, and the
+    backward through both. (B, S, H, 128) bf16 in and out."""
+
+    def __init__(self, positions: torch.Tensor, eps: float = NORM_EPS,
+                 scale: Optional[float] = None):
+        self.rope = ops.Rope(positions)
+        self.eps = eps
+        self.scale = scale
+
+    def __call__(self, q, k, v, wq, wk):
+        return _SingleAttention.apply(q, k, v, wq, wk, self.rope, self.eps, self.scale)
+
+
+class _SingleAttention(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, wq, wk, rope, eps, scale):
+        q_r = ops.qk_norm_rope(None, q, None, wq, rope, eps=eps)
+        k_r = ops.qk_norm_rope(None, k, None, wk, rope, eps=eps)
+        v_c = v.contiguous()
+        o, lse = ops.attn_fwd(q_r, k_r, v_c, scale=scale)
+        ctx.save_for_backward(q, k, wq, wk, q_r, k_r, v_c, o, lse)
+        ctx.rope, ctx.eps, ctx.scale = rope, eps, scale
+        return o
+
+    @staticmethod
+    def backward(ctx, d_o):
+        q, k, wq, wk, q_r, k_r, v_c, o, lse = ctx.saved_tensors
+        dq_r, dk_r, dv = ops.attn_bwd(q_r, k_r, v_c, o, d_o.contiguous(), lse, scale=ctx.scale)
+        _, dq, _, dwq = ops.qk_norm_rope_bwd(None, q, None, wq, ctx.rope, dq_r, eps=ctx.eps)
+        _, dk, _, dwk = ops.qk_norm_rope_bwd(None, k, None, wk, ctx.rope, dk_r, eps=ctx.eps)
+        return dq, dk, dv, dwq.to(wq.dtype), dwk.to(wk.dtype), None, None, None
+
+
+JointFn = Callable[..., Tuple[torch.Tensor, torch.Tensor]]
+SingleFn = Callable[..., torch.Tensor]
+
+
+# ---------------------------------------------------------------- blocks
+
+@dataclass
+class BlockShape:
+    dim: int
+    heads: int
+    head_dim: int = 128
+
+
+def double_block(w: Weights, img: torch.Tensor, txt: torch.Tensor, temb: torch.Tensor,
+                 attention: JointFn, shape: BlockShape, *, prefix: str = "double",
+                 lora_scale: float = 1.0,
+                 acts: Optional[Dict[str, torch.Tensor]] = None) -> Tuple[torch.Tensor,
+                                                                          torch.Tensor]:
+    """One double-stream block (lib.rs:301-392). img (B, I, dim), txt (B, T,
+    dim), temb (dim,). `attention(q_t, k_t, v_t, q_i, k_i, v_i, wq_t, wk_t,
+    wq_i, wk_i)` gets the projections (B, len, H, head_dim) before the q/k
+    RMSNorm and returns the (o_t, o_i) attention outputs."""
+    d, h, hd = shape.dim, shape.heads, shape.head_dim
+    if f"weights/{prefix}.mod.weight" in w:
+        mi = mt = _modulation(w, f"{prefix}.mod", temb, d, lora_scale)
+    else:
+        mi = _modulation(w, f"{prefix}.img.mod", temb, d, lora_scale)
+        mt = _modulation(w, f"{prefix}.txt.mod", temb, d, lora_scale)
+    B, I, T = img.shape[0], img.shape[1], txt.shape[1]
+
+    ih = layer_norm_mod(img, mi[0], mi[1])
+    th = layer_norm_mod(txt, mt[0], mt[1])
+    if acts is not None:
+        acts[f"{prefix}.img_norm1"], acts[f"{prefix}.txt_norm1"] = ih, th
+
+    def proj(stream, x, n, which):
+        return linear(w, f"{prefix}.{stream}.to_{which}", x, lora_scale).reshape(B, n, h, hd)
+
+    q_i, k_i, v_i = (proj("img", ih, I, c) for c in ("q", "k", "v"))
+    q_t, k_t, v_t = (proj("txt", th, T, c) for c in ("q", "k", "v"))
+    a_t, a_i = attention(q_t, k_t, v_t, q_i, k_i, v_i,
+                         _get(w, f"weights/{prefix}.txt_q_norm.weight"),
+                         _get(w, f"weights/{prefix}.txt_k_norm.weight"),
+                         _get(w, f"weights/{prefix}.img_q_norm.weight"),
+                         _get(w, f"weights/{prefix}.img_k_norm.weight"))
+    if acts is not None:
+        acts[f"{prefix}.attn_img"] = a_i
+
+    img = img + mi[2] * linear(w, f"{prefix}.img.to_out", a_i.reshape(B, I, d), lora_scale)
+    txt = txt + mt[2] * linear(w, f"{prefix}.txt.to_out", a_t.reshape(B, T, d), lora_scale)
+    if acts is not None:
+        acts[f"{prefix}.img_post_attn"] = img
+
+    ih2 = layer_norm_mod(img, mi[3], mi[4])
+    th2 = layer_norm_mod(txt, mt[3], mt[4])
+    img = img + mi[5] * _mlp(w, f"{prefix}.img.mlp", ih2, lora_scale)
+    txt = txt + mt[5] * _mlp(w, f"{prefix}.txt.mlp", th2, lora_scale)
+    if acts is not None:
+        acts[f"{prefix}.img_out"], acts[f"{prefix}.txt_out"] = img, txt
+    return img, txt
+
+
+def single_block(w: Weights, x: torch.Tensor, temb: torch.Tensor, attention: SingleFn,
+                 shape: BlockShape, *, prefix: str = "single", lora_scale: float = 1.0,
+                 acts: Optional[Dict[str, torch.Tensor]] = None) -> torch.Tensor:
+    """One single-stream block (lib.rs:394-456): fused QKV with LoRA, q/k
+    RMSNorm + RoPE, attention, SwiGLU from the same normed input, gated
+    residuals (x + g_at * attn + g_mlp * mlp; this block has no output
+    projection and no second adaLN). x (B, S, dim); `attention(q, k, v, wq,
+    wk)` gets the projections before the norm."""
+    d, h, hd = shape.dim, shape.heads, shape.head_dim
+    sh1, sc1, g_at, _, _, g_mlp = _modulation(w, f"{prefix}.mod", temb, d, lora_scale)
+    B, S = x.shape[0], x.shape[1]
+    nh = layer_norm_mod(x, sh1, sc1)
+    if acts is not None:
+        acts[f"{prefix}.norm1"] = nh
+    qkv = linear(w, f"{prefix}.to_qkv", nh, lora_scale).reshape(B, S, 3, h, hd)
+    q, k, v = qkv.unbind(2)
+    o = attention(q, k, v, _get(w, f"weights/{prefix}.q_norm.weight"),
+                  _get(w, f"weights/{prefix}.k_norm.weight"))
+    a = o.reshape(B, S, d)
+    if acts is not None:
+        acts[f"{prefix}.attn"] = a
+    m = _mlp(w, f"{prefix}.mlp", nh, lora_scale)
+    if acts is not None:
+        acts[f"{prefix}.mlp"] = m
+    out = x + g_at * a + g_mlp * m
+    if acts is not None:
+        acts[f"{prefix}.out"] = out
+    return out
+
+
+# ---------------------------------------------------------------- AdamW
+
+@dataclass
+class AdamW:
+    """Bias-corrected AdamW, weight decay 0 (lib.rs:465-505): fp32 moments,
+    step = lr * m_hat / (sqrt(v_hat) + eps), parameter updated in its own
+    dtype."""
+    lr: float = 1e-3
+    beta1: float = 0.9
+    beta2: float = 0.999
+    eps: float = 1e-8
+
+    def init(self, params: List[torch.Tensor]) -> List[Tuple[torch.Tensor, torch.Tensor]]:
+        return [(torch.zeros_like(p, dtype=torch.float32),
+                 torch.zeros_like(p, dtype=torch.float32)) for p in params]
+
+    @torch.no_grad()
+    def step(self, params: List[torch.Tensor], grads: List[torch.Tensor],
+             state: List[Tuple[torch.Tensor, torch.Tensor]], t: int) -> None:
+        bc1 = 1.0 - self.beta1 ** t
+        bc2 = 1.0 - self.beta2 ** t
+        for p, g, (m, v) in zip(params, grads, state):
+            g = g.float()
+            m.mul_(self.beta1).add_(g * (1.0 - self.beta1))
+            v.mul_(self.beta2).add_(g * g * (1.0 - self.beta2))
+            denom = torch.sqrt(v / bc2) + self.eps
+            p.copy_((p.float() - (m / bc1) / denom * self.lr).to(p.dtype))
+
+
+# ------------------------------------------- the benchmark configuration
+
+def make_c3_weights(dim: int = 3072, heads: int = 24, rank: int = 16, seed: int = 0,
+                    device=None, dtype=torch.bfloat16) -> Weights:
+    """Random-init weights of the FLUX-style double block of the LoRA
+    configuration: base weights ~N(0, 0.02), no biases, modulation per
+    stream, q/k norm weights 1, a 4x GELU MLP per stream, LoRA rank `rank` on
+    q/k/v/out of both streams with A ~N(0, 1/dim) and B = 0. Drawn from one
+    CPU generator in key order, then moved."""
+    g = torch.Generator().manual_seed(seed)
+    w: Weights = {}
+
+    def add(name, out_f, in_f, std=0.02):
+        w[f"weights/{name}.weight"] = torch.randn(out_f, in_f, generator=g) * std
+
+    for s in ("img", "txt"):
+        add(f"double.{s}.mod", 6 * dim, dim)
+        for c in ("q", "k", "v", "out"):
+            add(f"double.{s}.to_{c}", dim, dim)
+            w[f"weights/double.{s}.to_{c}.lora_a"] = (torch.randn(rank, dim, generator=g)
+                                                      / math.sqrt(dim))
+            w[f"weights/double.{s}.to_{c}.lora_b"] = torch.zeros(dim, rank)
+        add(f"double.{s}.mlp.fc1", 4 * dim, dim)
+        add(f"double.{s}.mlp.fc2", dim, 4 * dim)
+        w[f"weights/double.{s}_q_norm.weight"] = torch.ones(128)
+        w[f"weights/double.{s}_k_norm.weight"] = torch.ones(128)
+    return {k: v.to(device=device, dtype=dtype) for k, v in w.items()}
+
+
+def lora_keys(w: Weights) -> List[str]:
+    return sorted(k for k in w if k.endswith(".lora_a") or k.endswith(".lora_b"))
+
+
+def joint_positions(txt_len: int, grid: int) -> torch.Tensor:
+    """(T + G*G, 4) axial positions of the joint sequence: text at 0, image
+    token i at (0, i // G, i % G, 0)."""
+    pos = torch.zeros((txt_len + grid * grid, 4), dtype=torch.float32)
+    i = torch.arange(grid * grid)
+    pos[txt_len:, 1] = (i // grid).float()
+    pos[txt_len:, 2] = (i % grid).float()
+    return pos
+
+
+class LoraTrainer:
+    """One LoRA training step of a double block: forward, MSE loss against
+    targets, backward to the LoRA factors only, AdamW. `attention` defaults
+    to the B200 op (JointAttention at `positions`)."""
+
+    def __init__(self, w: Weights, shape: BlockShape, positions: torch.Tensor, *,
+                 lora_scale: float = 1.0, opt: Optional[AdamW] = None,
+                 attention: Optional[JointFn] = None, grad_hook=None):
+        self.w = dict(w)
+        self.shape = shape
+        self.lora_scale = lora_scale
+        self.keys = lora_keys(w)
+        self.params = [self.w[k] for k in self.keys]
+        for p in self.params:
+            p.requires_grad_(True)
+        self.opt = opt if opt is not None else AdamW()
+        self.state = self.opt.init(self.params)
+        self.t = 0
+        self.attention = attention if attention is not None else attn.JointAttention(
+            positions.to(self.params[0].device))
+        self.grad_hook = grad_hook  # e.g. an all-reduce of the LoRA grads across replicas
+
+    def loss(self, img, txt, temb, target_img, target_txt):
+        o_i, o_t = double_block(self.w, img, txt, temb, self.attention, self.shape,
+                                lora_scale=self.lora_scale)
+        return mse(o_i, target_img) + mse(o_t, target_txt)
+
+    def step(self, img, txt, temb, target_img, target_txt) -> torch.Tensor:
+        loss = self.loss(img, txt, temb, target_img, target_txt)
+        grads = torch.autograd.grad(loss, self.params)
+        if self.grad_hook is not None:
+            grads = self.grad_hook(grads)
+        self.t += 1
+        self.opt.step(self.params, grads, self.state, self.t)
+        return loss.detach()

@@ -33,6 +33,10 @@ Outputs (float32 arrays; bf16 values are exact in float32):
       generator's own `apply_rope` + `attention` + torch autograd
       (gen_block.py:98-119) on seeded inputs: an end-to-end golden for the
       op with the rotation inside.
+  block_fixture.npz
+      the double + single block pair (weights, inputs, activations, loss,
+      LoRA/input gradients, AdamW states) for the block replay (see
+      block_fixture below).
 """
 from __future__ import annotations
 
@@ -151,7 +155,50 @@ def main(ref_root: str) -> None:
     np.savez_compressed(HERE / "attn_rope_fixture_fp32.npz",
                         q=q.numpy(), k=k.numpy(), v=v.numpy(), dout=dout.numpy(), pos=pos.numpy(),
                         o=o.detach().numpy(), dq=dq.numpy(), dk=dk.numpy(), dv=dv.numpy())
+    block_fixture(fx, gb)
     print("wrote", sorted(p.name for p in HERE.glob("*.npz")))
+
+
+# activations the block replay compares (gen_block.py:199-247, 266-290, 361-362)
+BLOCK_ACTS = ("double.img_norm1", "double.txt_norm1", "double.attn_img", "double.img_post_attn",
+              "double.img_out", "double.txt_out", "single.norm1", "single.attn", "single.mlp",
+              "single.out", "output/img", "output/txt", "loss")
+
+
+def block_fixture(fx: Path, gb) -> None:
+    """block_fixture.npz: the whole double + single block pair of the
+    fixtures (gen_block.py:297-411) for a replay of the reference's block
+    test (src/bin/block_backward.rs): the fp32 weights and inputs (the bf16
+    run draws the same values and casts them, checked here), the recorded
+    activations, loss, LoRA and input gradients and the AdamW states after 1
+    and 10 steps of both runs (`<tag>:<key>`), and the axial positions.
+    Keys use ':' where the fixture has '/'."""
+    from safetensors.torch import load_file
+    w32 = load_file(str(fx / "block_fp32.safetensors"))
+    w16 = load_file(str(fx / "block_bf16.safetensors"))
+    out = {}
+    for k, t in w32.items():
+        if k.startswith(("weights/", "inputs/")):
+            assert torch.equal(w16[k], t.to(torch.bfloat16)), k
+            out[k.replace("/", ":")] = t.numpy()
+    for tag, src in (("fp32", w32), ("bf16", w16)):
+        for k, t in src.items():
+            if k in BLOCK_ACTS or k.startswith(("grad/double.", "grad/single.", "grad/inputs/",
+                                                "opt1/", "opt10/")):
+                out[f"{tag}:{k.replace('/', ':')}"] = t.float().numpy()
+    cfg = gb.CONFIG
+    g, tl = cfg["img_grid"], cfg["txt_len"]
+    rows = torch.arange(g * g) // g
+    cols = torch.arange(g * g) % g
+    z = torch.zeros(g * g)
+    zt = torch.zeros(tl)
+    out["pos_img"] = torch.stack([rows.float(), cols.float(), z, z], dim=-1).numpy()
+    out["pos_txt"] = torch.stack([torch.arange(tl).float(), zt, zt, zt], dim=-1).numpy()
+    out["config"] = np.array([cfg["dim"], cfg["heads"], cfg["head_dim"], cfg["lora_rank"]],
+                             dtype=np.int64)
+    out["lora_scale"] = np.array(cfg["lora_alpha"] / cfg["lora_rank"], dtype=np.float64)
+    out["adamw"] = np.array([cfg["lr"], *cfg["adamw_betas"], cfg["adamw_eps"]], dtype=np.float64)
+    np.savez_compressed(HERE / "block_fixture.npz", **out)
 
 
 if __name__ == "__main__":
