@@ -1,6 +1,6 @@
 """Benchmark of the joint-attention forward + backward on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c4|c5] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c3|c4|c5] [--impl ours|reference]
                     [--ncu-case]
 
 A step is one forward + backward of the op (axial RoPE inside) over one
@@ -190,13 +190,173 @@ def run_reference(args, cfg, rank):
     print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------- C3: LoRA block
+C3_METRIC = "LoRA train steps/s (C3 double-stream block: fwd + bwd to the LoRA factors + AdamW)"
+
+
+def run_block(args, rank, world, local):
+    """C3: one FLUX-style double-stream block (dim 3072, 24 x 128 heads, 512
+    text + 64x64 image tokens, 4x GELU MLPs, per-stream adaLN), rank-16
+    LoRA (alpha 16) on q/k/v/out of both streams, bf16, random-init weights
+    (blocks.make_c3_weights). A step is forward, MSE loss against seeded
+    targets, backward to the LoRA factors only, and AdamW; with N ranks each
+    runs a replica on its own seeded batch and the LoRA gradients are
+    averaged with one NCCL all-reduce per step (weak scaling; `value` counts
+    every replica's steps)."""
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable":
+                              "the reference's block step is Candle (Rust, not buildable here); "
+                              "its CPU arithmetic is timed by --config c2 --impl reference"}),
+                  flush=True)
+        return
+    import torch
+    import torch.distributed as dist
+
+    from foundry_trainer_b200 import _lib, blocks, ops
+    import ctypes as C
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    dim, heads, rank_lora, txt_len, grid = 3072, 24, 16, 512, 64
+    shape = blocks.BlockShape(dim=dim, heads=heads)
+    w = blocks.make_c3_weights(dim, heads, rank_lora, seed=0, device=dev)
+    g = torch.Generator().manual_seed(1 + rank)
+    mk = lambda *sh: torch.randn(*sh, generator=g).to(device=dev, dtype=torch.bfloat16)
+    img, txt, temb = mk(1, grid * grid, dim), mk(1, txt_len, dim), mk(dim)
+    t_img, t_txt = mk(1, grid * grid, dim), mk(1, txt_len, dim)
+
+    def allreduce(grads):
+        flat = torch.cat([x.float().reshape(-1) for x in grads])
+        dist.all_reduce(flat)
+        flat /= world
+        out, o = [], 0
+        for x in grads:
+            out.append(flat[o:o + x.numel()].view_as(x).to(x.dtype))
+            o += x.numel()
+        return out
+
+    tr = blocks.LoraTrainer(w, shape, blocks.joint_positions(txt_len, grid),
+                            lora_scale=1.0, grad_hook=allreduce if world > 1 else None)
+    step = lambda: tr.step(img, txt, temb, t_img, t_txt)
+    flush_buf = torch.empty(256 * 1024 * 1024 // 4, device=dev, dtype=torch.float32)
+    lib = _lib.load()
+    sampler = ClockSampler(local)
+    sampler.start()
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    if ops.device_status() != 0:
+        raise RuntimeError("device-side bounded wait expired during warm-up")
+    K = args.steps
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    lib.fa_timing_enable(1)
+    for kid in (0, 1):
+        lib.fa_timing_read(kid, C.byref(C.c_double()), C.byref(C.c_int()))
+    t_region0 = time.time()
+    for i in range(K):
+        flush_buf.zero_()
+        starts[i].record()
+        loss = step()
+        ends[i].record()
+    torch.cuda.synchronize()
+    t_region1 = time.time()
+    lib.fa_timing_enable(0)
+    kt = {}
+    for kid, name in ((0, "fwd"), (1, "bwd")):
+        ms, n = C.c_double(), C.c_int()
+        lib.fa_timing_read(kid, C.byref(ms), C.byref(n))
+        kt[name] = ms.value / max(n.value, 1)
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop(t_region0, t_region1)
+    if ops.device_status() != 0:
+        raise RuntimeError("device-side bounded wait expired while timing")
+    step_ms = sum(a.elapsed_time(b) for a, b in zip(starts, ends))
+    t = torch.tensor([step_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    step_ms_max = t.item()
+
+    # end to end: every step's img, txt, temb, targets in from pinned host
+    # memory and the loss out
+    e2e = None
+    if not args.no_e2e:
+        host = [x.cpu().pin_memory() for x in (img, txt, temb, t_img, t_txt)]
+        dbuf = [torch.empty_like(x) for x in (img, txt, temb, t_img, t_txt)]
+        h_loss = torch.empty((), dtype=torch.float32).pin_memory()
+        h2d = sum(x.numel() * x.element_size() for x in host)
+        for _ in range(2):
+            for d_, h_ in zip(dbuf, host):
+                d_.copy_(h_, non_blocking=True)
+            h_loss.copy_(tr.step(*dbuf), non_blocking=True)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(K):
+            for d_, h_ in zip(dbuf, host):
+                d_.copy_(h_, non_blocking=True)
+            h_loss.copy_(tr.step(*dbuf), non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        te = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e = {"value": world * K / (te.item() / 1e3), "unit": "steps/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
+               "path": "blocks.LoraTrainer.step with pinned host inputs and the loss read back"}
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    peaks = _peaks()
+    S = txt_len + grid * grid
+    attn_bwd_flops = 10.0 * heads * S * S * 128
+    line = {
+        "metric": C3_METRIC, "value": world * K / (step_ms_max / 1e3), "unit": "steps/s",
+        "n_gpus": world, "steps": K, "warmup": max(args.warmup, 3),
+        "ms_per_step": step_ms_max / K, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded: hidden, temb, targets ~ N(0,1); weights ~ N(0,0.02), "
+                "LoRA A ~ N(0,1/3072), B = 0)",
+        "config": {"workload": f"c3: double-stream block dim {dim}, {heads}x128 heads, "
+                               f"{txt_len} text + {grid}x{grid} image tokens, 4x GELU MLP, "
+                               f"LoRA r{rank_lora} alpha 16 on q/k/v/out of both streams",
+                   "parallelism": f"data-parallel x{world} (LoRA grads all-reduced)",
+                   "l2": "flushed between timed steps (256 MB write outside the step events)"},
+        "roofline": {"kernel": "attn_bwd_kernel", "bound": "tensor",
+                     "achieved": attn_bwd_flops / (kt["bwd"] / 1e3) / 1e12 if kt["bwd"] else None,
+                     "peak": peaks["bf16"], "unit": "TFLOP/s",
+                     "frac": (attn_bwd_flops / (kt["bwd"] / 1e3) / 1e12 / peaks["bf16"]
+                              if kt["bwd"] else None),
+                     "traffic": None, "peak_source": f"{peaks['source']} bf16",
+                     "fwd_kernel_ms": kt["fwd"], "bwd_kernel_ms": kt["bwd"]},
+        "cpu_baseline": None,
+        "e2e": e2e,
+        # per step: q, k prologues + v concat + fwd; dO concat + delta + bwd +
+        # dQ finish + q, k prologue backwards
+        "gpu_launches": 10 * K,
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+
+
 # ------------------------------------------------------------------- ours
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="c2", choices=["c1", "c2", "c4", "c5"])
+    ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--transport", default="peer", choices=["peer", "nccl"],
                     help="c5 exchange: peer memory (copy-engine pulls, peer stores, device "
@@ -217,8 +377,11 @@ def main():
     local = _env_int("LOCAL_RANK", 0)
 
     from foundry_trainer_b200 import configs
-    cfg = configs.CONFIGS[args.config]
+    cfg = configs.CONFIGS.get(args.config)
 
+    if args.config == "c3":
+        run_block(args, rank, world, local)
+        return
     if args.impl == "reference":
         run_reference(args, cfg, rank)
         return
