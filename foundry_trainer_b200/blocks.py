@@ -10,6 +10,7 @@ weight dictionary keyed like its fixtures and its `Weights` map
   layer_norm_mod    lib.rs:60-71    LayerNorm in fp32, (1 + scale) * n + shift, cast
   double_block      lib.rs:301-392
   single_block      lib.rs:394-456
+  single_block_fused bin/throughput.rs:577-629 (the klein single block)
   mse               lib.rs:458-463
   AdamW             lib.rs:472-505  fp32 moments, bias-corrected, weight decay 0
 
@@ -99,12 +100,20 @@ def _mlp(w: Weights, name: str, x: torch.Tensor, lora_scale: float) -> torch.Ten
     return swiglu(w, name, x, lora_scale)
 
 
+def modulation_sets(w: Weights, name: str, temb_silu: torch.Tensor, dim: int, sets: int,
+                    lora_scale: float = 1.0) -> List[torch.Tensor]:
+    """The 3*sets (dim,) chunks (shift, scale, gate per set) of
+    linear(temb_silu) (bin/throughput.rs:297-324; lib.rs:310-317 with two
+    sets). Constant across steps when temb is."""
+    out = linear(w, name, temb_silu.reshape(1, dim), lora_scale).reshape(3 * sets * dim)
+    return list(out.split(dim))
+
+
 def _modulation(w: Weights, name: str, temb: torch.Tensor, dim: int,
                 lora_scale: float) -> List[torch.Tensor]:
     """The six (dim,) chunks of linear(silu(temb)): shift1, scale1, gate1,
     shift2, scale2, gate2 (the reference feeds silu(temb), lib.rs:310-317)."""
-    out = linear(w, name, F.silu(temb).reshape(1, dim), lora_scale).reshape(6 * dim)
-    return list(out.split(dim))
+    return modulation_sets(w, name, F.silu(temb), dim, 2, lora_scale)
 
 
 # ------------------------------------------------------ attention callables
@@ -161,14 +170,20 @@ class BlockShape:
 def double_block(w: Weights, img: torch.Tensor, txt: torch.Tensor, temb: torch.Tensor,
                  attention: JointFn, shape: BlockShape, *, prefix: str = "double",
                  lora_scale: float = 1.0,
-                 acts: Optional[Dict[str, torch.Tensor]] = None) -> Tuple[torch.Tensor,
-                                                                          torch.Tensor]:
+                 acts: Optional[Dict[str, torch.Tensor]] = None,
+                 mods: Optional[Tuple[List[torch.Tensor], List[torch.Tensor]]] = None
+                 ) -> Tuple[torch.Tensor, torch.Tensor]:
     """One double-stream block (lib.rs:301-392). img (B, I, dim), txt (B, T,
     dim), temb (dim,). `attention(q_t, k_t, v_t, q_i, k_i, v_i, wq_t, wk_t,
     wq_i, wk_i)` gets the projections (B, len, H, head_dim) before the q/k
-    RMSNorm and returns the (o_t, o_i) attention outputs."""
+    RMSNorm and returns the (o_t, o_i) attention outputs. `mods` = the
+    image and text streams' six modulation chunks when they are computed once
+    for a whole stack (bin/throughput.rs:480-572); otherwise they come from
+    this block's modulation linear(s)."""
     d, h, hd = shape.dim, shape.heads, shape.head_dim
-    if f"weights/{prefix}.mod.weight" in w:
+    if mods is not None:
+        mi, mt = mods
+    elif f"weights/{prefix}.mod.weight" in w:
         mi = mt = _modulation(w, f"{prefix}.mod", temb, d, lora_scale)
     else:
         mi = _modulation(w, f"{prefix}.img.mod", temb, d, lora_scale)
@@ -235,6 +250,29 @@ def single_block(w: Weights, x: torch.Tensor, temb: torch.Tensor, attention: Sin
     if acts is not None:
         acts[f"{prefix}.out"] = out
     return out
+
+
+def single_block_fused(w: Weights, x: torch.Tensor, mod3: List[torch.Tensor],
+                       attention: SingleFn, shape: BlockShape, *, mlp_ratio: int = 3,
+                       prefix: str = "single", lora_scale: float = 1.0) -> torch.Tensor:
+    """The single-stream block in the klein layout (bin/throughput.rs:577-629):
+    one fused in-projection `<prefix>.to_in` (dim -> (3 + 2*mlp_ratio)*dim:
+    Q, K, V, then the SwiGLU gate and up of mlp_ratio*dim each), attention,
+    silu(gate) * up, and one fused out-projection `<prefix>.to_out` over
+    [attention | activation] (dim + mlp_ratio*dim -> dim); one gate on its
+    output: x + g * out. mod3 = (shift, scale, gate)."""
+    d, h, hd = shape.dim, shape.heads, shape.head_dim
+    sh, sc, g = mod3
+    B, S = x.shape[0], x.shape[1]
+    nh = layer_norm_mod(x, sh, sc)
+    fused = linear(w, f"{prefix}.to_in", nh, lora_scale).reshape(B, S, 3 + 2 * mlp_ratio, d)
+    q, k, v = (fused[:, :, c].reshape(B, S, h, hd) for c in range(3))
+    gate = fused[:, :, 3:3 + mlp_ratio].reshape(B, S, mlp_ratio * d)
+    up = fused[:, :, 3 + mlp_ratio:].reshape(B, S, mlp_ratio * d)
+    o = attention(q, k, v, _get(w, f"weights/{prefix}.q_norm.weight"),
+                  _get(w, f"weights/{prefix}.k_norm.weight"))
+    joined = torch.cat([o.reshape(B, S, d), F.silu(gate) * up], dim=-1)
+    return x + g * linear(w, f"{prefix}.to_out", joined, lora_scale)
 
 
 # ---------------------------------------------------------------- AdamW

@@ -116,3 +116,35 @@ def test_product_attention_fails_loudly_on_cpu():
     with pytest.raises(Exception):
         blocks.double_block(w, img, txt, torch.zeros(256, dtype=torch.bfloat16),
                             attn.JointAttention(pos), blocks.BlockShape(256, 2))
+
+
+def test_single_block_fused_layout():
+    # the klein single block against a direct composition of its parts
+    torch.manual_seed(5)
+    d, h, mr, S = 256, 2, 3, 24
+    shape = blocks.BlockShape(dim=d, heads=h)
+    g = torch.Generator().manual_seed(7)
+    w = {"weights/single.0.to_in.weight": torch.randn((3 + 2 * mr) * d, d, generator=g) * 0.02,
+         "weights/single.0.to_in.lora_a": torch.randn(4, d, generator=g) * 0.02,
+         "weights/single.0.to_in.lora_b": torch.randn((3 + 2 * mr) * d, 4, generator=g) * 0.02,
+         "weights/single.0.to_out.weight": torch.randn(d, d + mr * d, generator=g) * 0.02,
+         "weights/single.0.q_norm.weight": torch.rand(128, generator=g) + 0.5,
+         "weights/single.0.k_norm.weight": torch.rand(128, generator=g) + 0.5,
+         "weights/mod_single.weight": torch.randn(3 * d, d, generator=g) * 0.02}
+    x = torch.randn(1, S, d, generator=g)
+    temb = torch.randn(d, generator=g)
+    mod3 = blocks.modulation_sets(w, "mod_single", torch.nn.functional.silu(temb), d, 1)
+    att = bs.TorchSingleAttention(blocks.joint_positions(8, 4), torch.float32)
+    out = blocks.single_block_fused(w, x, mod3, att, shape, mlp_ratio=mr, prefix="single.0")
+
+    sh, sc, gt = mod3
+    nh = blocks.layer_norm_mod(x, sh, sc)
+    W_in = w["weights/single.0.to_in.weight"] + (w["weights/single.0.to_in.lora_b"]
+                                                 @ w["weights/single.0.to_in.lora_a"])
+    fused = nh @ W_in.T
+    q, k, v = (fused[..., i * d:(i + 1) * d].reshape(1, S, h, 128) for i in range(3))
+    gate, up = fused[..., 3 * d:(3 + mr) * d], fused[..., (3 + mr) * d:]
+    o = att(q, k, v, w["weights/single.0.q_norm.weight"], w["weights/single.0.k_norm.weight"])
+    ref = x + gt * (torch.cat([o.reshape(1, S, d), torch.nn.functional.silu(gate) * up], -1)
+                    @ w["weights/single.0.to_out.weight"].T)
+    assert bs.rel_l2(out, ref) <= 1e-5
