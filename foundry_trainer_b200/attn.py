@@ -119,18 +119,48 @@ class _JointAttention(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, do_t, do_i):
-        (q_t, k_t, q_i, k_i, wq_t, wk_t, wq_i, wk_i, q_j, k_j, v_j, o_j,
-         lse) = ctx.saved_tensors
-        T = ctx.T
-        do_j = ops.qk_norm_rope(do_t.contiguous(), do_i.contiguous(), None, None, None)
-        dq_j, dk_j, dv_j = ops.attn_bwd(q_j, k_j, v_j, o_j, do_j, lse, scale=ctx.scale)
-        dq_t, dq_i, dwq_t, dwq_i = ops.qk_norm_rope_bwd(q_t, q_i, wq_t, wq_i, ctx.rope, dq_j,
-                                                        eps=ctx.eps)
-        dk_t, dk_i, dwk_t, dwk_i = ops.qk_norm_rope_bwd(k_t, k_i, wk_t, wk_i, ctx.rope, dk_j,
-                                                        eps=ctx.eps)
-        cast = lambda g, w: g.to(w.dtype) if g is not None else None
-        return (dq_t, dk_t, dv_j[:, :T], dq_i, dk_i, dv_j[:, T:], cast(dwq_t, wq_t),
-                cast(dwk_t, wk_t), cast(dwq_i, wq_i), cast(dwk_i, wk_i), None, None, None)
+        return _joint_backward(ctx, do_t, do_i) + (None, None, None)
+
+
+def _joint_backward(ctx, do_t, do_i):
+    """Gradients of the ten tensor inputs of the joint attention from the
+    saved prologue inputs, the joint q/k/v, O and LSE."""
+    (q_t, k_t, q_i, k_i, wq_t, wk_t, wq_i, wk_i, q_j, k_j, v_j, o_j,
+     lse) = ctx.saved_tensors
+    T = ctx.T
+    do_j = ops.qk_norm_rope(do_t.contiguous(), do_i.contiguous(), None, None, None)
+    dq_j, dk_j, dv_j = ops.attn_bwd(q_j, k_j, v_j, o_j, do_j, lse, scale=ctx.scale)
+    dq_t, dq_i, dwq_t, dwq_i = ops.qk_norm_rope_bwd(q_t, q_i, wq_t, wq_i, ctx.rope, dq_j,
+                                                    eps=ctx.eps)
+    dk_t, dk_i, dwk_t, dwk_i = ops.qk_norm_rope_bwd(k_t, k_i, wk_t, wk_i, ctx.rope, dk_j,
+                                                    eps=ctx.eps)
+    cast = lambda g, w: g.to(w.dtype) if g is not None else None
+    return (dq_t, dk_t, dv_j[:, :T], dq_i, dk_i, dv_j[:, T:], cast(dwq_t, wq_t),
+            cast(dwk_t, wk_t), cast(dwq_i, wq_i), cast(dwk_i, wk_i))
+
+
+class _JointAttentionReuse(torch.autograd.Function):
+    """The joint attention with O and LSE given (kept from an earlier,
+    graph-free forward on the same inputs): the prologue runs again for the
+    backward's joint q/k/v, the attention forward does not."""
+
+    @staticmethod
+    def forward(ctx, q_t, k_t, v_t, q_i, k_i, v_i, wq_t, wk_t, wq_i, wk_i, kept, rope, eps,
+                scale):
+        # `kept` = (O, LSE) as a tuple: not an autograd input, so the outputs
+        # are views of a tensor this node owns, as in _JointAttention
+        o_j, lse = kept
+        T = q_t.shape[1]
+        q_j = ops.qk_norm_rope(q_t, q_i, wq_t, wq_i, rope, eps=eps)
+        k_j = ops.qk_norm_rope(k_t, k_i, wk_t, wk_i, rope, eps=eps)
+        v_j = ops.qk_norm_rope(v_t, v_i, None, None, None)
+        ctx.save_for_backward(q_t, k_t, q_i, k_i, wq_t, wk_t, wq_i, wk_i, q_j, k_j, v_j, o_j, lse)
+        ctx.rope, ctx.eps, ctx.scale, ctx.T = rope, eps, scale, T
+        return o_j[:, :T], o_j[:, T:]
+
+    @staticmethod
+    def backward(ctx, do_t, do_i):
+        return _joint_backward(ctx, do_t, do_i) + (None, None, None, None)
 
 
 class JointAttention:
@@ -152,3 +182,32 @@ class JointAttention:
     def __call__(self, q_t, k_t, v_t, q_i, k_i, v_i, wq_t, wk_t, wq_i, wk_i):
         return _JointAttention.apply(q_t, k_t, v_t, q_i, k_i, v_i, wq_t, wk_t, wq_i, wk_i,
                                      self.rope, self.eps, self.scale)
+
+
+class CheckpointedJointAttention(JointAttention):
+    """JointAttention for gradient-checkpointed blocks: in a graph-free
+    forward (torch.no_grad) it keeps the joint O and LSE; the next call with
+    gradients enabled — the block's recompute during the checkpointed
+    backward, on the same inputs — reuses them and skips the attention
+    forward (the LSE makes the recompute unnecessary; the backward needs only
+    O, LSE and the joint q/k/v). Each block needs its own instance."""
+
+    def __init__(self, positions: torch.Tensor, eps: float = ops.NORM_EPS,
+                 scale: Optional[float] = None):
+        super().__init__(positions, eps, scale)
+        self.kept = None
+
+    def __call__(self, q_t, k_t, v_t, q_i, k_i, v_i, wq_t, wk_t, wq_i, wk_i):
+        if not torch.is_grad_enabled():
+            q_j = ops.qk_norm_rope(q_t, q_i, wq_t, wq_i, self.rope, eps=self.eps)
+            k_j = ops.qk_norm_rope(k_t, k_i, wk_t, wk_i, self.rope, eps=self.eps)
+            v_j = ops.qk_norm_rope(v_t, v_i, None, None, None)
+            o_j, lse = ops.attn_fwd(q_j, k_j, v_j, scale=self.scale)
+            self.kept = (o_j, lse)
+            T = q_t.shape[1]
+            return o_j[:, :T], o_j[:, T:]
+        if self.kept is not None:
+            kept, self.kept = self.kept, None
+            return _JointAttentionReuse.apply(q_t, k_t, v_t, q_i, k_i, v_i, wq_t, wk_t, wq_i,
+                                              wk_i, kept, self.rope, self.eps, self.scale)
+        return super().__call__(q_t, k_t, v_t, q_i, k_i, v_i, wq_t, wk_t, wq_i, wk_i)

@@ -13,6 +13,8 @@ weight dictionary keyed like its fixtures and its `Weights` map
   single_block_fused bin/throughput.rs:577-629 (the klein single block)
   mse               lib.rs:458-463
   AdamW             lib.rs:472-505  fp32 moments, bias-corrected, weight decay 0
+  checkpointed_backward lib.rs:519-638 (stage-wise recompute; attention
+                    forward skipped with the kept O and LSE)
 
 The attention of each block is a callable (`attention=`): by default the
 B200 op with its fused q/k RMSNorm + RoPE prologue (`attn.JointAttention`
@@ -154,6 +156,46 @@ class _SingleAttention(torch.autograd.Function):
         return dq, dk, dv, dwq.to(wq.dtype), dwk.to(wk.dtype), None, None, None
 
 
+class CheckpointedSingleAttention(SingleAttention):
+    """SingleAttention for gradient-checkpointed blocks: keeps O and LSE in
+    a graph-free forward and reuses them (no attention forward) in the
+    recompute with gradients, like attn.CheckpointedJointAttention."""
+
+    def __init__(self, positions: torch.Tensor, eps: float = NORM_EPS,
+                 scale: Optional[float] = None):
+        super().__init__(positions, eps, scale)
+        self.kept = None
+
+    def __call__(self, q, k, v, wq, wk):
+        if not torch.is_grad_enabled():
+            q_r = ops.qk_norm_rope(None, q, None, wq, self.rope, eps=self.eps)
+            k_r = ops.qk_norm_rope(None, k, None, wk, self.rope, eps=self.eps)
+            o, lse = ops.attn_fwd(q_r, k_r, v.contiguous(), scale=self.scale)
+            self.kept = (o, lse)
+            return o
+        if self.kept is not None:
+            kept, self.kept = self.kept, None
+            return _SingleAttentionReuse.apply(q, k, v, wq, wk, kept, self.rope, self.eps,
+                                               self.scale)
+        return super().__call__(q, k, v, wq, wk)
+
+
+class _SingleAttentionReuse(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, wq, wk, kept, rope, eps, scale):
+        o, lse = kept  # a tuple: not an autograd input
+        q_r = ops.qk_norm_rope(None, q, None, wq, rope, eps=eps)
+        k_r = ops.qk_norm_rope(None, k, None, wk, rope, eps=eps)
+        v_c = v.contiguous()
+        ctx.save_for_backward(q, k, wq, wk, q_r, k_r, v_c, o, lse)
+        ctx.rope, ctx.eps, ctx.scale = rope, eps, scale
+        return o.view_as(o)
+
+    @staticmethod
+    def backward(ctx, d_o):
+        return _SingleAttention.backward(ctx, d_o)[:5] + (None,) * 4
+
+
 JointFn = Callable[..., Tuple[torch.Tensor, torch.Tensor]]
 SingleFn = Callable[..., torch.Tensor]
 
@@ -273,6 +315,54 @@ def single_block_fused(w: Weights, x: torch.Tensor, mod3: List[torch.Tensor],
                   _get(w, f"weights/{prefix}.k_norm.weight"))
     joined = torch.cat([o.reshape(B, S, d), F.silu(gate) * up], dim=-1)
     return x + g * linear(w, f"{prefix}.to_out", joined, lora_scale)
+
+
+# ------------------------------------------ checkpointed forward/backward
+
+Stage = Callable[[List[torch.Tensor]], List[torch.Tensor]]
+
+
+def checkpointed_backward(stages: List[Stage], inputs: List[torch.Tensor],
+                          seed: Callable[[List[torch.Tensor]], torch.Tensor],
+                          params: List[torch.Tensor]):
+    """Forward and backward keeping only each stage's inputs
+    (lib.rs:519-638). Forward: every stage runs graph-free, so its
+    intermediates are freed as it returns. Backward: stages in reverse; a
+    stage's saved inputs become leaves, the stage runs again with gradients,
+    and its upstream gradient enters through sum(out * upstream). Each
+    parameter (a LoRA factor) must belong to exactly one stage. Attention
+    callables that kept their O and LSE in the graph-free forward
+    (attn.CheckpointedJointAttention, CheckpointedSingleAttention) skip the
+    attention forward in the recompute.
+    Returns (loss, input gradients, {id(param): gradient})."""
+    if not stages:
+        raise ValueError("checkpointed_backward: no stages")
+    saved: List[List[torch.Tensor]] = []
+    cur = [x.detach() for x in inputs]
+    with torch.no_grad():
+        for st in stages:
+            saved.append(cur)
+            cur = [o.detach() for o in st(cur)]
+    outs = [o.requires_grad_(True) for o in cur]
+    loss = seed(outs)
+    upstream = list(torch.autograd.grad(loss, outs))
+    param_grads = {}
+    in_grads: List[torch.Tensor] = []
+    for k in range(len(stages) - 1, -1, -1):
+        leaves = [x.detach().requires_grad_(True) for x in saved[k]]
+        with torch.enable_grad():
+            o = stages[k](leaves)
+            if len(o) != len(upstream):
+                raise ValueError(f"stage {k} returned {len(o)} outputs, expected {len(upstream)}")
+            seeded = sum((a * g).sum() for a, g in zip(o, upstream))
+            g = torch.autograd.grad(seeded, leaves + params, allow_unused=True)
+        for p, gp in zip(params, g[len(leaves):]):
+            if gp is not None:
+                param_grads[id(p)] = gp
+        upstream = list(g[:len(leaves)])
+        if k == 0:
+            in_grads = upstream
+    return loss.detach(), in_grads, param_grads
 
 
 # ---------------------------------------------------------------- AdamW

@@ -148,3 +148,36 @@ def test_single_block_fused_layout():
     ref = x + gt * (torch.cat([o.reshape(1, S, d), torch.nn.functional.silu(gate) * up], -1)
                     @ w["weights/single.0.to_out.weight"].T)
     assert bs.rel_l2(out, ref) <= 1e-5
+
+
+def test_checkpointed_backward_matches_autograd_on_the_block_pair(fx):
+    # the reference's stage-wise checkpointing (lib.rs:519-638) over the
+    # fixture's double and single block: same loss, LoRA and input gradients
+    # as one autograd pass
+    dtype = torch.float32
+    run = _run(fx, "fp32")
+    params = [run.w[k] for k in run.lora]
+    for p in params:
+        p.requires_grad_(True)
+
+    def double(xs):
+        img2, txt2 = blocks.double_block(run.w, xs[0], xs[1], run.temb, run.joint, fx.shape,
+                                         lora_scale=fx.lora_scale)
+        return [torch.cat([txt2, img2], dim=1)]
+
+    def single(xs):
+        return [blocks.single_block(run.w, xs[0], run.temb, run.single, fx.shape,
+                                    lora_scale=fx.lora_scale)]
+
+    def seed(outs):
+        o = outs[0]
+        return blocks.mse(o[:, run.T:], run.target_img) + blocks.mse(o[:, :run.T], run.target_txt)
+
+    loss, in_grads, pg = blocks.checkpointed_backward([double, single], [run.img, run.txt],
+                                                       seed, params)
+    acts, ref = run.grads()
+    assert bs.rel_l2(loss.reshape(1), acts["loss"].reshape(1)) <= 1e-6
+    assert bs.rel_l2(in_grads[0][0], ref["grad/inputs/img"]) <= 1e-6
+    assert bs.rel_l2(in_grads[1][0], ref["grad/inputs/txt"]) <= 1e-6
+    for k, p in zip(run.lora, params):
+        assert bs.rel_l2(pg[id(p)], ref["grad/" + k[len("weights/"):]]) <= 1e-6, k
