@@ -191,6 +191,73 @@ def run_reference(args, cfg, rank):
 
 
 # --------------------------------------------------------- C3: LoRA block
+def cpu_block_sample(txt_len=512, grid=64, dim=3072, heads=24, rank_lora=16, head_chunk=4):
+    """One C3 LoRA step on the host cores: the block code of blocks.py in
+    fp32 torch, its joint attention and q/k prologue from the oracle port
+    (numpy, `head_chunk` heads at a time). Returns (steps/s, seconds)."""
+    import numpy as np
+    import torch
+
+    from foundry_trainer_b200 import blocks
+    from oracle import attn_oracle as orc
+
+    pos = blocks.joint_positions(txt_len, grid).numpy()
+    eps = blocks.NORM_EPS
+
+    def chunks(H):
+        return [list(range(i, min(i + head_chunk, H))) for i in range(0, H, head_chunk)]
+
+    class _OracleJoint(torch.autograd.Function):
+        @staticmethod
+        def forward(ctx, q_t, k_t, v_t, q_i, k_i, v_i, wq_t, wk_t, wq_i, wk_i):
+            T = q_t.shape[1]
+            n = lambda t: t[0].detach().numpy()
+            ins = [n(x) for x in (q_t, k_t, v_t, q_i, k_i, v_i)]
+            ws = [x.detach().numpy() for x in (wq_t, wk_t, wq_i, wk_i)]
+            q = np.concatenate([orc.qk_norm_rope(ins[0], ws[0], eps, pos[:T], "f32"),
+                                orc.qk_norm_rope(ins[3], ws[2], eps, pos[T:], "f32")], 0)
+            k = np.concatenate([orc.qk_norm_rope(ins[1], ws[1], eps, pos[:T], "f32"),
+                                orc.qk_norm_rope(ins[4], ws[3], eps, pos[T:], "f32")], 0)
+            v = np.concatenate([ins[2], ins[5]], 0)
+            o = np.concatenate([orc.attn_fwd(q[:, hs], k[:, hs], v[:, hs], "f32")
+                                for hs in chunks(q.shape[1])], 1)
+            ctx.np = (ins, ws, q, k, v, T)
+            return torch.from_numpy(o[:T])[None], torch.from_numpy(o[T:])[None]
+
+        @staticmethod
+        def backward(ctx, do_t, do_i):
+            ins, ws, q, k, v, T = ctx.np
+            d_o = np.concatenate([do_t[0].numpy(), do_i[0].numpy()], 0)
+            parts = [orc.attn_bwd(q[:, hs], k[:, hs], v[:, hs], d_o[:, hs], "f32")
+                     for hs in chunks(q.shape[1])]
+            dq, dk, dv = (np.concatenate([p[j] for p in parts], 1) for j in range(3))
+            dq_t, dwq_t = orc.qk_norm_rope_grad(ins[0], ws[0], eps, pos[:T], dq[:T], "f32")
+            dq_i, dwq_i = orc.qk_norm_rope_grad(ins[3], ws[2], eps, pos[T:], dq[T:], "f32")
+            dk_t, dwk_t = orc.qk_norm_rope_grad(ins[1], ws[1], eps, pos[:T], dk[:T], "f32")
+            dk_i, dwk_i = orc.qk_norm_rope_grad(ins[4], ws[3], eps, pos[T:], dk[T:], "f32")
+            t = lambda a: torch.from_numpy(np.ascontiguousarray(a))[None]
+            w_ = lambda a: torch.from_numpy(np.ascontiguousarray(a))
+            return (t(dq_t), t(dk_t), t(dv[:T]), t(dq_i), t(dk_i), t(dv[T:]), w_(dwq_t),
+                    w_(dwk_t), w_(dwq_i), w_(dwk_i))
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    w = blocks.make_c3_weights(dim, heads, rank_lora, seed=0, dtype=torch.float32)
+    g = torch.Generator().manual_seed(1)
+    img, txt = torch.randn(1, grid * grid, dim, generator=g), torch.randn(1, txt_len, dim,
+                                                                          generator=g)
+    temb = torch.randn(dim, generator=g)
+    t_img, t_txt = torch.randn(1, grid * grid, dim, generator=g), torch.randn(1, txt_len, dim,
+                                                                              generator=g)
+    tr = blocks.LoraTrainer(w, blocks.BlockShape(dim, heads), torch.from_numpy(pos),
+                            attention=_OracleJoint.apply)
+    t0 = time.perf_counter()
+    loss = tr.step(img, txt, temb, t_img, t_txt)
+    dt = time.perf_counter() - t0
+    if not torch.isfinite(loss):
+        raise RuntimeError("cpu block sample: non-finite loss")
+    return 1.0 / dt, dt
+
+
 C3_METRIC = "LoRA train steps/s (C3 double-stream block: fwd + bwd to the LoRA factors + AdamW)"
 
 
@@ -318,6 +385,12 @@ def run_block(args, rank, world, local):
         dist.destroy_process_group()
     if rank != 0:
         return
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        v_cpu, secs = cpu_block_sample()
+        cpu = {"value": v_cpu, "unit": "steps/s", "cores": os.cpu_count(), "kind": "port",
+               "sample": f"one whole C3 LoRA step (fp32 torch block code, numpy oracle "
+                         f"attention and q/k prologue), {secs:.1f} s"}
     peaks = _peaks()
     S = txt_len + grid * grid
     attn_bwd_flops = 10.0 * heads * S * S * 128
@@ -340,7 +413,7 @@ def run_block(args, rank, world, local):
                               if kt["bwd"] else None),
                      "traffic": None, "peak_source": f"{peaks['source']} bf16",
                      "fwd_kernel_ms": kt["fwd"], "bwd_kernel_ms": kt["bwd"]},
-        "cpu_baseline": None,
+        "cpu_baseline": cpu,
         "e2e": e2e,
         # per step: q, k prologues + v concat + fwd; dO concat + delta + bwd +
         # dQ finish + q, k prologue backwards

@@ -31,3 +31,10 @@ def test_reference_arm_line():
 def test_block_config_reference_arm_is_declared_unavailable():
     d = _run("--impl", "reference", "--config", "c3")
     assert d["impl"] == "reference" and "unavailable" in d
+
+
+def test_block_cpu_baseline_sample_runs_small():
+    sys.path.insert(0, str(ROOT))
+    import bench
+    steps_per_s, secs = bench.cpu_block_sample(txt_len=8, grid=4, dim=256, heads=2, rank_lora=4)
+    assert steps_per_s > 0 and secs > 0
