@@ -112,3 +112,148 @@ def peer_rank(rank, world, port, arrays, results, steps=1, copy="ce"):
         if ex is not None:
             ex.close()
         dist.destroy_process_group()
+
+
+# ------------------------------------------------- gloo (CPU) stand-ins
+class _NoStream:
+    """Stream stand-in for CPU ranks: ordering is program order."""
+
+    def wait_stream(self, other):
+        pass
+
+    def wait_event(self, event):
+        pass
+
+
+class _NoEvent:
+    def __init__(self, *args, **kwargs):
+        pass
+
+    def record(self, stream=None):
+        pass
+
+
+class GlooExchange:
+    """PeerExchange's surface for CPU ranks of a gloo group: the published
+    shards move by an all-gather at the forward's barrier, the dK/dV rows
+    each rank stored for the owners by an all-gather at the backward's
+    barrier. The addresses the backward scatters to are (par, owner, src,
+    which) handles the stand-in kernels resolve."""
+
+    def __init__(self, shape, dtype=torch.float32):
+        import torch.distributed as dist
+        self.dist = dist
+        self.world, self.rank = dist.get_world_size(), dist.get_rank()
+        self.shape = tuple(shape)
+        self.copy_stream, self.side_stream = _NoStream(), _NoStream()
+        self.n_fwd = self.n_bwd = 0
+        self._pub = [[torch.zeros(self.shape, dtype=dtype) for _ in range(2)] for _ in range(2)]
+        self._recv = [torch.zeros((self.world, 2) + self.shape) for _ in range(2)]
+        self._gathered = [None, None]
+        self.outbox = {}
+
+    def pub(self, par):
+        return tuple(self._pub[par])
+
+    def recv(self, par):
+        return self._recv[par]
+
+    def recv_ptrs(self, par, which):
+        return [(par, owner, self.rank, which) for owner in range(self.world)]
+
+    def barrier(self, channel, stream=None):
+        dist, W = self.dist, self.world
+        if channel == 0:
+            par = (self.n_fwd - 1) % 2
+            mine = torch.stack(self._pub[par])
+            got = [torch.empty_like(mine) for _ in range(W)]
+            dist.all_gather(got, mine)
+            self._gathered[par] = got
+        else:
+            par = (self.n_bwd - 1) % 2
+            mine = torch.stack([torch.stack([self.outbox[(par, o, self.rank, w)] for w in (0, 1)])
+                                for o in range(W)])  # (owner, which, B, S, H, D)
+            got = [torch.empty_like(mine) for _ in range(W)]
+            dist.all_gather(got, mine)
+            for src in range(W):
+                self._recv[par][src] = got[src][self.rank]
+        dist.barrier()
+
+    def pull(self, par, src, slot, which, dst, stream):
+        S = self.shape[1]
+        dst[:, slot * S:(slot + 1) * S].copy_(self._gathered[par][src][which])
+
+
+def fake_peer_kernels(ex):
+    from tests.ring_support import FakeRingKernels, _rope_np
+
+    class FakePeerKernels(FakeRingKernels):
+        """peer.PeerKernels' surface on CPU tensors, float64 arithmetic, in
+        the conventions of the C ABI calls (fa_fwd_fold, fa_merge_f32,
+        fa_bwd_scatter, fa_reduce_cast_f32)."""
+
+        def fwd_fold(self, q, k, v, scale, o_acc, lse_acc, step, last, o, lse, stream=None):
+            super().fwd_fold(q, k, v, scale, o_acc, lse_acc, step, last, o, lse)
+
+        def merge(self, o_a, lse_a, o_b, lse_b, o, lse):
+            self.calls.append("merge")
+            a, b = lse_a.double(), lse_b.double()
+            m = torch.maximum(a, b)
+            wa, wb = torch.exp(a - m), torch.exp(b - m)
+            tr = lambda x: x.permute(0, 2, 1)[..., None]
+            o.copy_((o_a.double() * tr(wa) + o_b.double() * tr(wb)) / tr(wa + wb))
+            lse.copy_(m + torch.log(wa + wb))
+
+        def bwd_scatter(self, q, k_all, v_all, d_o, lse2_pad, delta_pad, dq_acc, seg,
+                        dk_ptrs, dv_ptrs, scale):
+            B, S, H, D = q.shape
+            kv = k_all.shape[1]
+            dk = torch.empty((B, kv, H, D))
+            dv = torch.empty((B, kv, H, D))
+            self.bwd_partial(q, k_all, v_all, d_o, lse2_pad, delta_pad, dq_acc, dk, dv, scale,
+                             False)
+            for i, (hk, hv) in enumerate(zip(dk_ptrs, dv_ptrs)):
+                ex.outbox[hk] = dk[:, i * seg:(i + 1) * seg].clone()
+                ex.outbox[hv] = dv[:, i * seg:(i + 1) * seg].clone()
+
+        def reduce_cast(self, recv, pos, dk, dv):
+            self.calls.append("reduce_cast")
+            sk = recv[:, 0].double().sum(0)
+            if pos is not None:
+                sk = _rope_np(sk.float(), pos, inverse=True).double()
+            dk.copy_(sk)
+            dv.copy_(recv[:, 1].double().sum(0))
+
+    return FakePeerKernels()
+
+
+def peer_gloo_rank(rank, world, port, shape, seed, results, steps=2):
+    """One gloo rank: the peer-memory schedule (peer.peer_fwd / peer_bwd) of
+    its shard with the CPU stand-ins; the last step's results are reported."""
+    import torch.distributed as dist
+
+    from foundry_trainer_b200 import ops, peer
+    from tests.ring_support import full_problem
+
+    torch.cuda.current_stream = lambda *a, **k: _NoStream()
+    torch.cuda.Event = _NoEvent
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=120))
+    try:
+        B, S, H, D = shape
+        q, k, v, d_o, pos = full_problem(B, S, H, D, seed)
+        n = S // world
+        sl = slice(rank * n, (rank + 1) * n)
+        qs, ks, vs, dos = (t[:, sl].contiguous() for t in (q, k, v, d_o))
+        ps = pos[sl].contiguous()
+        ex = GlooExchange((B, n, H, D))
+        kern = fake_peer_kernels(ex)
+        scale = ops.default_scale(D)
+        for _ in range(steps):
+            o, lse, q_r, k_all, v_all = peer.peer_fwd(qs, ks, vs, ps, scale, ex, kern)
+            dq, dk, dv = peer.peer_bwd(q_r, k_all, v_all, o, dos, lse, ps, scale, ex, kern)
+        results.put((rank, o.numpy(), dq.numpy(), dk.numpy(), dv.numpy(), kern.calls))
+    finally:
+        dist.destroy_process_group()

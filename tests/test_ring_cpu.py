@@ -95,3 +95,46 @@ def test_peer_layout_regions_are_disjoint_and_aligned():
         assert all(a[1] <= b[0] for a, b in zip(spans, spans[1:]))
         assert spans[-1][1] <= lay.total
         assert all(a % 16 == 0 for a, _ in spans)
+
+
+def _run_peer(world, shape, seed):
+    from tests import peer_support
+    ctx = mp.get_context("spawn")
+    results = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=peer_support.peer_gloo_rank,
+                         args=(r, world, port, shape, seed, results)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = {}
+    try:
+        for _ in range(world):
+            r, *vals = results.get(timeout=240)
+            got[r] = vals
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    return [got[r] for r in range(world)]
+
+
+@pytest.mark.parametrize("world,S", [(2, 96), (3, 105)])
+def test_peer_schedule_matches_single_sequence_oracle(world, S):
+    # the peer-memory schedule (foundry_trainer_b200/peer.py: fold order and
+    # groups, the two accumulators and their merge, the backward's scatter to
+    # the owners and their sums) on gloo ranks with CPU stand-ins for the
+    # device calls and the exchange
+    from tests import ring_support
+    B, H, D = 1, 2, 128
+    q, k, v, d_o, pos = ring_support.full_problem(B, S, H, D, seed=10 + world)
+    o_ref, _, dq_ref, dk_ref, dv_ref = orc.attn_fwd_bwd_bshd(
+        q.numpy(), k.numpy(), v.numpy(), d_o.numpy(), "f32", rope_pos=pos.numpy())
+    shards = _run_peer(world, (B, S, H, D), seed=10 + world)
+    cat = lambda i: np.concatenate([s[i] for s in shards], axis=1)
+    for name, ours, ref in (("o", cat(0), o_ref), ("dq", cat(1), dq_ref), ("dk", cat(2), dk_ref),
+                            ("dv", cat(3), dv_ref)):
+        assert orc.max_rel(ours, ref) <= TOL, (name, orc.max_rel(ours, ref))
+    calls = shards[0][4]
+    assert calls.count("merge") == 2 and calls.count("reduce_cast") == 2  # two steps
