@@ -296,18 +296,8 @@ def run_block(args, rank, world, local):
     img, txt, temb = mk(1, grid * grid, dim), mk(1, txt_len, dim), mk(dim)
     t_img, t_txt = mk(1, grid * grid, dim), mk(1, txt_len, dim)
 
-    def allreduce(grads):
-        flat = torch.cat([x.float().reshape(-1) for x in grads])
-        dist.all_reduce(flat)
-        flat /= world
-        out, o = [], 0
-        for x in grads:
-            out.append(flat[o:o + x.numel()].view_as(x).to(x.dtype))
-            o += x.numel()
-        return out
-
-    tr = blocks.LoraTrainer(w, shape, blocks.joint_positions(txt_len, grid),
-                            lora_scale=1.0, grad_hook=allreduce if world > 1 else None)
+    tr = blocks.LoraTrainer(w, shape, blocks.joint_positions(txt_len, grid), lora_scale=1.0,
+                            grad_hook=blocks.allreduce_mean if world > 1 else None)
     step = lambda: tr.step(img, txt, temb, t_img, t_txt)
     flush_buf = torch.empty(256 * 1024 * 1024 // 4, device=dev, dtype=torch.float32)
     lib = _lib.load()

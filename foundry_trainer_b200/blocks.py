@@ -437,6 +437,21 @@ def joint_positions(txt_len: int, grid: int) -> torch.Tensor:
     return pos
 
 
+def allreduce_mean(grads, group=None):
+    """Data-parallel replicas: the mean of each LoRA gradient over the ranks
+    of `group`, with one all-reduce of one fp32 buffer."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    flat = torch.cat([g.float().reshape(-1) for g in grads])
+    dist.all_reduce(flat, group=group)
+    flat /= world
+    out, o = [], 0
+    for g in grads:
+        out.append(flat[o:o + g.numel()].view_as(g).to(g.dtype))
+        o += g.numel()
+    return out
+
+
 class LoraTrainer:
     """One LoRA training step of a double block: forward, MSE loss against
     targets, backward to the LoRA factors only, AdamW. `attention` defaults

@@ -193,3 +193,45 @@ def rel_l2(a: torch.Tensor, b: torch.Tensor) -> float:
 def cosine(a: torch.Tensor, b: torch.Tensor) -> float:
     a, b = a.detach().double().flatten(), b.detach().double().flatten()
     return float((a @ b) / (a.norm() * b.norm() + 1e-30))
+
+
+def dp_gloo_rank(rank, world, port, steps, results):
+    """One data-parallel replica of the LoRA block step on a gloo group (CPU,
+    torch stand-in attention): its own seeded batch, gradients averaged by
+    blocks.allreduce_mean; reports the LoRA factors after `steps` steps."""
+    import os
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
+    try:
+        tr, batches = dp_problem(world)
+        tr.grad_hook = blocks.allreduce_mean
+        for _ in range(steps):
+            tr.step(*batches[rank])
+        results.put((rank, {k: p.detach().clone() for k, p in zip(tr.keys, tr.params)}))
+    finally:
+        dist.destroy_process_group()
+
+
+def dp_problem(world):
+    """A small FLUX-style block (dim 256, 2 heads) with the stand-in attention
+    and one seeded batch per replica."""
+    w = blocks.make_c3_weights(dim=256, heads=2, rank=4, seed=3, dtype=torch.float32)
+    g = torch.Generator().manual_seed(11)
+    for k in w:
+        if k.endswith(".lora_b"):  # non-zero B so every factor moves from step 1
+            w[k] = torch.randn(w[k].shape, generator=g) * 0.01
+    pos = blocks.joint_positions(8, 4)
+    tr = blocks.LoraTrainer(w, blocks.BlockShape(256, 2), pos,
+                            attention=TorchJointAttention(pos, torch.float32))
+    batches = []
+    for r in range(world):
+        gr = torch.Generator().manual_seed(100 + r)
+        batches.append((torch.randn(1, 16, 256, generator=gr), torch.randn(1, 8, 256, generator=gr),
+                        torch.randn(256, generator=gr), torch.randn(1, 16, 256, generator=gr),
+                        torch.randn(1, 8, 256, generator=gr)))
+    return tr, batches

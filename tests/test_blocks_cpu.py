@@ -181,3 +181,40 @@ def test_checkpointed_backward_matches_autograd_on_the_block_pair(fx):
     assert bs.rel_l2(in_grads[1][0], ref["grad/inputs/txt"]) <= 1e-6
     for k, p in zip(run.lora, params):
         assert bs.rel_l2(pg[id(p)], ref["grad/" + k[len("weights/"):]]) <= 1e-6, k
+
+
+def test_data_parallel_lora_replicas_on_gloo_match_averaged_gradients():
+    import multiprocessing as mp
+    import socket
+    world, steps = 2, 3
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    results = ctx.Queue()
+    procs = [ctx.Process(target=bs.dp_gloo_rank, args=(r, world, port, steps, results))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    got = {}
+    try:
+        for _ in range(world):
+            r, params = results.get(timeout=240)
+            got[r] = params
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert all(p.exitcode == 0 for p in procs)
+    # one process: the mean of the replicas' gradients, the same AdamW steps
+    tr, batches = bs.dp_problem(world)
+    for _ in range(steps):
+        per = [torch.autograd.grad(tr.loss(*b), tr.params) for b in batches]
+        mean = [sum(gs) / world for gs in zip(*per)]
+        tr.t += 1
+        tr.opt.step(tr.params, mean, tr.state, tr.t)
+    for k, p in zip(tr.keys, tr.params):
+        for r in range(world):
+            assert bs.rel_l2(got[r][k], p) <= 1e-5, (r, k)
+    assert all(torch.equal(got[0][k], got[1][k]) for k in tr.keys)
