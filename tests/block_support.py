@@ -198,7 +198,8 @@ def cosine(a: torch.Tensor, b: torch.Tensor) -> float:
 def dp_gloo_rank(rank, world, port, steps, results):
     """One data-parallel replica of the LoRA block step on a gloo group (CPU,
     torch stand-in attention): its own seeded batch, gradients averaged by
-    blocks.allreduce_mean; reports the LoRA factors after `steps` steps."""
+    blocks.allreduce_mean; reports the first step's averaged gradients and
+    the LoRA factors after `steps` steps."""
     import os
     from datetime import timedelta
 
@@ -209,10 +210,20 @@ def dp_gloo_rank(rank, world, port, steps, results):
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
     try:
         tr, batches = dp_problem(world)
-        tr.grad_hook = blocks.allreduce_mean
+        seen = []
+
+        def hook(grads):
+            avg = blocks.allreduce_mean(grads)
+            seen.append([g.clone() for g in avg])
+            return avg
+
+        tr.grad_hook = hook
         for _ in range(steps):
             tr.step(*batches[rank])
-        results.put((rank, {k: p.detach().clone() for k, p in zip(tr.keys, tr.params)}))
+        # numpy by value: tensors would be shared by file descriptor, which
+        # dies with this process
+        results.put((rank, [g.numpy() for g in seen[0]],
+                     {k: p.detach().numpy().copy() for k, p in zip(tr.keys, tr.params)}))
     finally:
         dist.destroy_process_group()
 
