@@ -377,7 +377,8 @@ def peer_bwd(q_r, k_all, v_all, o, d_o, lse, pos, scale, ex: PeerExchange, kern:
     order = block_order(ex.rank, W)
     dk_ptrs, dv_ptrs = ex.recv_ptrs(par, 0), ex.recv_ptrs(par, 1)
     kern.bwd_scatter(q_r, k_all, v_all, d_o, lse2_pad, delta_pad, dq_acc, S,
-                     [dk_ptrs[o] for o in order], [dv_ptrs[o] for o in order], scale)
+                     [dk_ptrs[owner] for owner in order], [dv_ptrs[owner] for owner in order],
+                     scale)
     _mark(trace, "scatter")
     if W > 1:
         ex.barrier(1)  # every rank's contribution to this rank's keys has landed
