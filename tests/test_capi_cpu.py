@@ -75,3 +75,54 @@ def test_loading_missing_library_fails_loudly(tmp_path, monkeypatch):
     monkeypatch.setattr(_lib, "LIB_PATH", tmp_path / "nope.so")
     with pytest.raises(_lib.FaError):
         _lib.load()
+
+
+def test_peer_exchange_entry_points_validate_without_a_gpu():
+    from foundry_trainer_b200 import _lib
+    lib = _lib.load()
+    INV, ALIGN, TOO_LARGE = _lib.FA_ERR_INVALID_ARG, _lib.FA_ERR_ALIGNMENT, _lib.FA_ERR_TOO_LARGE
+    assert lib.fa_peer_flags_bytes() >= 4 * (4 * 8 + 4)  # arrive[4][8] + epoch[4] words
+    h = _lib.fa_peer_handle_t()
+    p = C.c_void_p()
+    assert lib.fa_peer_alloc(0, C.byref(p), C.byref(h)) == INV
+    assert lib.fa_peer_open(None, C.byref(p)) == INV
+    assert lib.fa_peer_close(None) == INV and lib.fa_peer_free(None) == INV
+    # copies: nothing to do, null pointers, pitch below width, misalignment, rows
+    assert lib.fa_copy_2d(None, 0, None, 0, 0, 1, None) == _lib.FA_OK
+    assert lib.fa_copy_2d(None, 64, None, 64, 64, 1, None) == INV
+    assert lib.fa_copy_2d(16, 32, 16, 64, 64, 1, None) == INV
+    assert lib.fa_copy_2d_sm(16, 64, 24, 64, 64, 1, 4, None) == ALIGN
+    assert lib.fa_copy_2d_sm(16, 64, 16, 64, 64, 70000, 4, None) == TOO_LARGE
+    assert lib.fa_copy_2d_sm(16, 64, 16, 64, 64, 1, 0, None) == INV
+    # barrier: world, rank and channel bounds, missing flag blocks
+    flags = (C.c_void_p * 9)(*([4096] * 9))
+    assert lib.fa_peer_barrier(0, 9, flags, 0, 1.0, None) == INV
+    assert lib.fa_peer_barrier(2, 2, flags, 0, 1.0, None) == INV
+    assert lib.fa_peer_barrier(0, 2, flags, 4, 1.0, None) == INV
+    assert lib.fa_peer_barrier(0, 2, flags, 0, 0.0, None) == INV
+    nul = (C.c_void_p * 2)(4096, None)
+    assert lib.fa_peer_barrier(0, 2, nul, 0, 1.0, None) == INV
+    assert lib.fa_peer_barrier(0, 1, flags, 0, 1.0, None) == _lib.FA_OK  # one rank: nothing
+    # scatter: segments must cover the keys exactly once, at most 8
+    t = _lib.fa_tensor_t(16, 0, 128, 128, 1)
+    seg = (C.c_void_p * 9)(*([4096] * 9))
+    args = lambda kv, s, n: (_lib.FA_DTYPE_BF16, 1, 256, kv, 1, 128, C.byref(t), C.byref(t),
+                             C.byref(t), C.byref(t), 4096, 4096, 4096, s, n, seg, seg, 0.1, None)
+    assert lib.fa_bwd_scatter(*args(512, 128, 2)) == INV    # 2 x 128 < 512 keys
+    assert lib.fa_bwd_scatter(*args(512, 256, 3)) == INV    # a segment past the keys
+    assert lib.fa_bwd_scatter(*args(2304, 256, 9)) == INV   # more than 8 segments
+    assert lib.fa_bwd_scatter(_lib.FA_DTYPE_F32, 1, 256, 512, 1, 128, None, None, None, None,
+                              None, None, None, 256, 2, seg, seg, 0.1,
+                              None) == _lib.FA_ERR_UNSUPPORTED
+    # reduce-cast and merge: head dim, parts, null and misaligned buffers
+    y = _lib.fa_tensor_t(4096, 128 * 4, 128, 128, 1)
+    assert lib.fa_reduce_cast_f32(_lib.FA_DTYPE_BF16, 1, 4, 1, 64, 4096, 4096, 2, 4096,
+                                  C.byref(y), None, 1.0, None, None) == _lib.FA_ERR_UNSUPPORTED
+    assert lib.fa_reduce_cast_f32(_lib.FA_DTYPE_BF16, 1, 4, 1, 128, 4096, 4096, 0, 4096,
+                                  C.byref(y), None, 1.0, None, None) == INV
+    assert lib.fa_reduce_cast_f32(_lib.FA_DTYPE_BF16, 1, 4, 1, 128, 4100, None, 2, 4096,
+                                  C.byref(y), None, 1.0, None, None) == ALIGN
+    assert lib.fa_merge_f32(_lib.FA_DTYPE_BF16, 1, 4, 1, 128, None, 4096, 4096, 4096,
+                            C.byref(y), 4096, None) == INV
+    assert lib.fa_merge_f32(_lib.FA_DTYPE_BF16, 1, 4, 1, 128, 4104, 4096, 4096, 4096,
+                            C.byref(y), 4096, None) == ALIGN
