@@ -4,11 +4,12 @@
                     [--ncu-case]
 
 A step is one forward + backward of the op (axial RoPE inside) over one
-synthetic batch of the named configuration, inputs resident in HBM. With N > 1
-(launched under torch.distributed.run, one rank per GPU) every rank runs its
-own batch x head partition of the workload with no collective on the data
-path (weak scaling); the timed region is bracketed by a barrier and a device
-synchronise, and the maximum time over ranks is reported. `--config c4` splits
+synthetic batch of the named configuration, inputs resident in HBM. The
+default workload is C2 on one GPU and C5 (below) on N > 1 GPUs (launched under
+torch.distributed.run, one rank per GPU); `--config c2` with N > 1 gives every
+rank its own C2 problem with no collective on the data path (weak scaling).
+The timed region is bracketed by a barrier and a device synchronise, and the
+maximum time over ranks is reported. `--config c4` splits
 its batch of 8 sequences over the ranks instead (strong scaling, still no
 cross-GPU traffic). `--config c5` runs
 the long-sequence case sequence-parallel instead: one sequence of 16896 rows
@@ -152,34 +153,53 @@ def cpu_oracle_sample(cfg, budget_s: float = 12.0, min_heads: int = 1):
     return flops / dt / 1e12, heads, dt, np.__version__
 
 
+def _oracle_rows_step(orc, qn, kn, vn, dn, pos, rows):
+    """One fp32 oracle fwd+bwd of one head for query rows [0, rows) against
+    every key (the reference's op graph, lib.rs:133-263, with the axial RoPE
+    of lib.rs:77-129 on q and k); returns its FLOPs, 14 * rows * S * D."""
+    cos, sin = orc.rope_tables(pos, "f32")
+    qr = orc.apply_rope(qn[:rows], cos[:rows], sin[:rows], "f32")
+    kr = orc.apply_rope(kn, cos, sin, "f32")
+    orc.attn_fwd(qr, kr, vn, "f32", return_lse=True)
+    dq, dk, dv = orc.attn_bwd(qr, kr, vn, dn[:rows], "f32")
+    orc.apply_rope_grad(dq, cos[:rows], sin[:rows], "f32")
+    orc.apply_rope_grad(dk, cos, sin, "f32")
+    return 14.0 * rows * kn.shape[0] * kn.shape[2]
+
+
 def run_reference(args, cfg, rank):
-    """The reference arm: the oracle port on the host cores, rank 0 only."""
+    """The reference arm: the oracle port on the host cores, rank 0 only.
+    A step is one head of the workload: the whole head when it is short
+    (C1, C2, C4 per sequence), else (C5) the query rows of one 2112-row
+    shard against all 16896 keys, so the run stays within a few minutes."""
     if rank != 0:
         return
-    import numpy as np  # noqa: F401
-
     from foundry_trainer_b200 import configs
     from oracle import attn_oracle as orc
     q, k, v, d_o = configs.make_inputs(cfg, batch=1)
     pos = configs.positions(cfg.txt, cfg.grid).numpy()
-    qn, kn, vn, dn = (t.float().numpy() for t in (q, k, v, d_o))
-    head = [0]
+    qn, kn, vn, dn = (t[0, :, :1].float().numpy() for t in (q, k, v, d_o))  # head 0 (S, 1, D)
+    rows = cfg.S if cfg.S <= 8192 else cfg.S // 8
     for _ in range(args.warmup):
-        orc.attn_fwd_bwd_bshd(qn, kn, vn, dn, "f32", heads=head, rope_pos=pos)
+        _oracle_rows_step(orc, qn, kn, vn, dn, pos, rows)
     t0 = time.perf_counter()
+    flops = 0.0
     for _ in range(args.steps):
-        orc.attn_fwd_bwd_bshd(qn, kn, vn, dn, "f32", heads=head, rope_pos=pos)
+        flops += _oracle_rows_step(orc, qn, kn, vn, dn, pos, rows)
     dt = time.perf_counter() - t0
-    flops = 14.0 * 1 * cfg.S * cfg.S * cfg.D * args.steps
     value = flops / dt / 1e12
     cores = os.cpu_count()
-    sample = (f"1 of {cfg.H} heads of {cfg.name} (B=1, S={cfg.S}, D={cfg.D}) fwd+bwd per step, "
+    what = (f"1 of {cfg.H} heads" if rows == cfg.S else
+            f"query rows 0-{rows - 1} (one of {cfg.S // rows} shards) of 1 of {cfg.H} heads "
+            f"against all {cfg.S} keys")
+    sample = (f"{what} of {cfg.name} (B=1, S={cfg.S}, D={cfg.D}) fwd+bwd per step, "
               f"fp32 numpy restatement of lib.rs:133-263 with RoPE (Candle CPU build unavailable: "
               f"no Rust toolchain)")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": dt * 1000.0 / args.steps, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": dt * 1000.0 / args.steps, "higher_is_better": True,
+        "scaling": "strong" if cfg.name in ("c4", "c5") else "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, configs.make_inputs)",
         "config": {"workload": cfg.name, "B": cfg.B, "H": cfg.H, "S": cfg.S, "D": cfg.D,
                    "txt": cfg.txt, "img_grid": cfg.grid, "rope": "axial (t,h,w,l), theta 10000"},
@@ -419,7 +439,10 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
+    ap.add_argument("--config", default=None, choices=["c1", "c2", "c3", "c4", "c5"],
+                    help="workload; default c2 on one GPU (BASELINE's headline "
+                         "configuration) and c5 on N > 1 (one 16896-row sequence "
+                         "sharded over the ranks: the sequence-parallel NVLink path)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--transport", default="peer", choices=["peer", "nccl"],
                     help="c5 exchange: peer memory (copy-engine pulls, peer stores, device "
@@ -432,12 +455,18 @@ def main():
     ap.add_argument("--ncu-case", action="store_true",
                     help="run --warmup eager fwd+bwd steps of --config and exit (no timing): "
                          "the small case ncu captures")
+    ap.add_argument("--timeline", action="store_true",
+                    help="c5 peer transport: run four eager steps with device events at the "
+                         "schedule's milestones and print every rank's milestones of the last "
+                         "one (ms since the rank's own step start), then exit")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
     rank = _env_int("RANK", 0)
     world = _env_int("WORLD_SIZE", 1)
     local = _env_int("LOCAL_RANK", 0)
+    if args.config is None:
+        args.config = "c2" if world == 1 else "c5"
 
     from foundry_trainer_b200 import configs
     cfg = configs.CONFIGS.get(args.config)
@@ -486,11 +515,14 @@ def main():
             def make_step(q, k, v, d_o):
                 outs = {}
 
-                def step():
-                    o_, lse_, q_r, k_all, v_all = peer.peer_fwd(q, k, v, pos, scale, ex, pkern)
+                def step(trace=None):
+                    # the status word is checked around the timed region, not per call
+                    o_, lse_, q_r, k_all, v_all = peer.peer_fwd(q, k, v, pos, scale, ex, pkern,
+                                                                trace, check_status=False)
                     outs["o"] = o_
                     outs["dq"], outs["dk"], outs["dv"] = peer.peer_bwd(
-                        q_r, k_all, v_all, o_, d_o, lse_, pos, scale, ex, pkern)
+                        q_r, k_all, v_all, o_, d_o, lse_, pos, scale, ex, pkern, trace,
+                        check_status=False)
                 return step, outs
         else:
             comm, kern = ring.RingComm(), ring.RingKernels()
@@ -536,6 +568,33 @@ def main():
     step, outs = make_step(q, k, v, d_o)
     flush_buf = torch.empty(256 * 1024 * 1024 // 4, device=dev, dtype=torch.float32)
     lib = _lib.load()
+
+    if args.timeline:
+        if not (ring_mode and args.transport == "peer"):
+            raise SystemExit("--timeline traces the c5 peer-memory schedule (--config c5)")
+        trace: list = []
+        for _ in range(4):
+            trace.clear()
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
+            step(trace)
+            torch.cuda.synchronize()
+        if ops.device_status() != 0:
+            raise RuntimeError("device-side bounded wait expired")
+        t0 = trace[0][1]
+        rows = [(name, t0.elapsed_time(e)) for name, e in trace]
+        allrows = [rows]
+        if world > 1:
+            allrows = [None] * world
+            dist.all_gather_object(allrows, rows)
+        if rank == 0:
+            for r, rr in enumerate(allrows):
+                print(f"rank {r}: " + " ".join(f"{nm}={t:.3f}" for nm, t in rr), flush=True)
+        ex.close()
+        if world > 1:
+            dist.destroy_process_group()
+        return
 
     if args.ncu_case:
         for _ in range(args.warmup):

@@ -11,7 +11,6 @@ from pathlib import Path
 
 _PKG = Path(__file__).resolve().parent
 LIB_PATH = _PKG / "lib" / "libfoundry_attn.so"
-SELFTEST_PATH = _PKG / "lib" / "libfa_selftest.so"
 
 FA_OK = 0
 FA_ERR_INVALID_ARG = 1
@@ -116,7 +115,6 @@ SIGNATURES = {
 }
 
 _lib = None
-_selftest = None
 
 
 def load() -> C.CDLL:
@@ -132,19 +130,6 @@ def load() -> C.CDLL:
             fn.argtypes = args
         _lib = lib
     return _lib
-
-
-def load_selftest() -> C.CDLL:
-    global _selftest
-    if _selftest is None:
-        if not SELFTEST_PATH.exists():
-            raise FaError(-1, "load", f"{SELFTEST_PATH} is missing; run the build")
-        st = C.CDLL(str(SELFTEST_PATH))
-        st.fa_selftest_umma.restype = C.c_int
-        st.fa_selftest_umma.argtypes = [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
-                                        C.c_void_p]
-        _selftest = st
-    return _selftest
 
 
 def status_string(status: int) -> str:

@@ -184,13 +184,57 @@ class JointAttention:
                                      self.rope, self.eps, self.scale)
 
 
+_PROBE_ROWS = 64
+
+
+def kept_key(inputs, weights):
+    """Identity of one call's inputs, stored with the O and LSE a graph-free
+    forward keeps and compared by `kept_matches` before they are reused.
+
+    The recompute of a checkpointed stage makes fresh projection tensors
+    (new storage, possibly at an address an unrelated tensor held before),
+    so storage addresses cannot tell the recompute of the same forward from
+    another call. The key holds instead: each input's shape, dtype and
+    device; each weight's storage and version (the weights are the same
+    tensors, unchanged, between a forward and its recompute); and an exact
+    copy of about 64 evenly spaced sequence rows of each input (all heads and
+    head-dim entries of those rows)."""
+    def probe(t):
+        t = t.detach()
+        step = max(1, t.shape[1] // _PROBE_ROWS)
+        return t[:, ::step].clone()
+
+    return (tuple((tuple(t.shape), t.dtype, t.device) for t in inputs),
+            tuple((w.data_ptr(), w._version, tuple(w.shape)) for w in weights),
+            tuple(probe(t) for t in inputs))
+
+
+def kept_matches(key, inputs, weights) -> bool:
+    """True when `inputs` / `weights` are, by kept_key's test, those the key
+    was taken from (one device synchronisation for the row comparison)."""
+    if key is None:
+        return False
+    meta, wid, probes = key
+    if meta != tuple((tuple(t.shape), t.dtype, t.device) for t in inputs):
+        return False
+    if wid != tuple((w.data_ptr(), w._version, tuple(w.shape)) for w in weights):
+        return False
+    now = kept_key(inputs, ())[2]
+    return all(torch.equal(a, b) for a, b in zip(probes, now))
+
+
 class CheckpointedJointAttention(JointAttention):
     """JointAttention for gradient-checkpointed blocks: in a graph-free
     forward (torch.no_grad) it keeps the joint O and LSE; the next call with
     gradients enabled — the block's recompute during the checkpointed
     backward, on the same inputs — reuses them and skips the attention
     forward (the LSE makes the recompute unnecessary; the backward needs only
-    O, LSE and the joint q/k/v). Each block needs its own instance."""
+    O, LSE and the joint q/k/v). The kept values are reused only when the
+    call's inputs pass `kept_matches` against the forward's (shapes, the
+    weights' identity and version, exact sampled rows of the six
+    projections); any other call runs the full forward. Each block should
+    have its own instance (a shared one is correct, but keeps only the last
+    forward's values)."""
 
     def __init__(self, positions: torch.Tensor, eps: float = ops.NORM_EPS,
                  scale: Optional[float] = None):
@@ -203,11 +247,13 @@ class CheckpointedJointAttention(JointAttention):
             k_j = ops.qk_norm_rope(k_t, k_i, wk_t, wk_i, self.rope, eps=self.eps)
             v_j = ops.qk_norm_rope(v_t, v_i, None, None, None)
             o_j, lse = ops.attn_fwd(q_j, k_j, v_j, scale=self.scale)
-            self.kept = (o_j, lse)
+            self.kept = (o_j, lse, kept_key((q_t, k_t, v_t, q_i, k_i, v_i),
+                                            (wq_t, wk_t, wq_i, wk_i)))
             T = q_t.shape[1]
             return o_j[:, :T], o_j[:, T:]
-        if self.kept is not None:
-            kept, self.kept = self.kept, None
+        kept, self.kept = self.kept, None
+        if kept is not None and kept_matches(kept[2], (q_t, k_t, v_t, q_i, k_i, v_i),
+                                             (wq_t, wk_t, wq_i, wk_i)):
             return _JointAttentionReuse.apply(q_t, k_t, v_t, q_i, k_i, v_i, wq_t, wk_t, wq_i,
-                                              wk_i, kept, self.rope, self.eps, self.scale)
+                                              wk_i, kept[:2], self.rope, self.eps, self.scale)
         return super().__call__(q_t, k_t, v_t, q_i, k_i, v_i, wq_t, wk_t, wq_i, wk_i)

@@ -159,7 +159,9 @@ class _SingleAttention(torch.autograd.Function):
 class CheckpointedSingleAttention(SingleAttention):
     """SingleAttention for gradient-checkpointed blocks: keeps O and LSE in
     a graph-free forward and reuses them (no attention forward) in the
-    recompute with gradients, like attn.CheckpointedJointAttention."""
+    recompute with gradients, like attn.CheckpointedJointAttention, and
+    under the same check (attn.kept_matches on q, k, v and the two norm
+    weights); any other call runs the full forward."""
 
     def __init__(self, positions: torch.Tensor, eps: float = NORM_EPS,
                  scale: Optional[float] = None):
@@ -171,11 +173,11 @@ class CheckpointedSingleAttention(SingleAttention):
             q_r = ops.qk_norm_rope(None, q, None, wq, self.rope, eps=self.eps)
             k_r = ops.qk_norm_rope(None, k, None, wk, self.rope, eps=self.eps)
             o, lse = ops.attn_fwd(q_r, k_r, v.contiguous(), scale=self.scale)
-            self.kept = (o, lse)
+            self.kept = (o, lse, attn.kept_key((q, k, v), (wq, wk)))
             return o
-        if self.kept is not None:
-            kept, self.kept = self.kept, None
-            return _SingleAttentionReuse.apply(q, k, v, wq, wk, kept, self.rope, self.eps,
+        kept, self.kept = self.kept, None
+        if kept is not None and attn.kept_matches(kept[2], (q, k, v), (wq, wk)):
+            return _SingleAttentionReuse.apply(q, k, v, wq, wk, kept[:2], self.rope, self.eps,
                                                self.scale)
         return super().__call__(q, k, v, wq, wk)
 

@@ -5,8 +5,9 @@
 
 Outputs (git-ignored, shipped with the tree to the GPU box):
     foundry_trainer_b200/lib/libfoundry_attn.so   the C ABI of include/foundry_attn.h
-    foundry_trainer_b200/lib/libfa_selftest.so    tcgen05 known-answer kernels (tests only)
     foundry_trainer_b200/lib/test_attn_op         C++ host-mirror driver (tests only)
+    tests/lib/libfa_selftest.so                   tcgen05 known-answer kernels of
+                                                  tests/csrc/ (tests only)
 """
 from __future__ import annotations
 
@@ -32,7 +33,9 @@ NVCC_FLAGS = ARCH + [
 LIB_SOURCES = ["capi.cu", "attn_fwd_sm100.cu", "attn_bwd_sm100.cu", "attn_f32.cu", "misc.cu", "peer.cu",
                "qk_prologue.cu",
                "noalloc.cu"]
-SELFTEST_SOURCES = ["umma_selftest.cu"]
+# test infrastructure: the descriptor / operand-layout known-answer kernels
+SELFTEST_SOURCES = [ROOT / "tests" / "csrc" / "umma_selftest.cu"]
+SELFTEST_LIB = ROOT / "tests" / "lib" / "libfa_selftest.so"
 
 
 def nvcc() -> str:
@@ -100,17 +103,18 @@ def build_all(force: bool = False, verbose_ptxas: bool = False) -> dict[str, Pat
     if force:
         for p in OBJ.glob("*.o"):
             p.unlink()
-    srcs = [CSRC / s for s in LIB_SOURCES + SELFTEST_SOURCES]
+    SELFTEST_LIB.parent.mkdir(exist_ok=True)
+    srcs = [CSRC / s for s in LIB_SOURCES] + SELFTEST_SOURCES
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
         objs = dict(zip([s.name for s in srcs], ex.map(lambda s: _compile(s, verbose_ptxas), srcs)))
     lib = LIB / "libfoundry_attn.so"
-    st = LIB / "libfa_selftest.so"
+    st = SELFTEST_LIB
     if force:
         for p in (lib, st):
             if p.exists():
                 p.unlink()
     _link([objs[s] for s in LIB_SOURCES], lib)
-    _link([objs[s] for s in SELFTEST_SOURCES], st)
+    _link([objs[s.name] for s in SELFTEST_SOURCES], st)
     drv = build_cpp_driver(force)
     return {"lib": lib, "selftest": st, "cpp_driver": drv}
 

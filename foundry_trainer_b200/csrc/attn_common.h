@@ -41,6 +41,10 @@ int record_cuda_error(cudaError_t e);
 // Sets the text fa_last_error() returns on this thread.
 void record_error_text(const char* msg);
 
+// Shape rules every attention entry point shares: dtype F32 or BF16, positive
+// sizes, head_dim 128, B and H within a grid dimension, B*S*H*D < 2^40.
+int check_attn_shape(int dtype, int B, int S, int H, int D);
+
 // Raises the dynamic shared-memory limit of `fn` once per (device, kernel).
 int ensure_smem_attr(const void* fn, int bytes, int kernel_id);
 

@@ -142,7 +142,7 @@ static int check_tensor(const fa_tensor_t* t, int esize, bool tma) {
   return FA_OK;
 }
 
-static int check_shape(int dtype, int B, int S, int H, int D) {
+int check_attn_shape(int dtype, int B, int S, int H, int D) {
   if (dtype != FA_DTYPE_F32 && dtype != FA_DTYPE_BF16) return FA_ERR_UNSUPPORTED;
   if (B <= 0 || S <= 0 || H <= 0 || D <= 0) return FA_ERR_INVALID_ARG;
   if (D != 128) return FA_ERR_UNSUPPORTED;
@@ -273,7 +273,7 @@ int fa_fwd(int dtype, int B, int S, int H, int D, const fa_tensor_t* q,
            const fa_tensor_t* k, const fa_tensor_t* v, const fa_tensor_t* o,
            float* lse, float scale, const fa_rope_t* rope, void* workspace,
            size_t workspace_bytes, void* stream) {
-  FA_TRY(check_shape(dtype, B, S, H, D));
+  FA_TRY(check_attn_shape(dtype, B, S, H, D));
   FA_TRY(check_rope(rope, D));
   if (!(scale > 0.f) || !std::isfinite(scale)) return FA_ERR_INVALID_ARG;
   const bool bf = dtype == FA_DTYPE_BF16;
@@ -331,7 +331,7 @@ int fa_bwd(int dtype, int B, int S, int H, int D, const fa_tensor_t* q,
            const fa_tensor_t* dk, const fa_tensor_t* dv, float scale,
            const fa_rope_t* rope, int deterministic, void* workspace,
            size_t workspace_bytes, void* stream) {
-  FA_TRY(check_shape(dtype, B, S, H, D));
+  FA_TRY(check_attn_shape(dtype, B, S, H, D));
   FA_TRY(check_rope(rope, D));
   if (!(scale > 0.f) || !std::isfinite(scale)) return FA_ERR_INVALID_ARG;
   const bool bf = dtype == FA_DTYPE_BF16;
@@ -415,7 +415,7 @@ int fa_bwd_saved(int dtype, int B, int S, int H, int D, const void* fwd_workspac
                  const fa_tensor_t* dk, const fa_tensor_t* dv, float scale,
                  const fa_rope_t* rope, void* workspace, size_t workspace_bytes,
                  void* stream) {
-  FA_TRY(check_shape(dtype, B, S, H, D));
+  FA_TRY(check_attn_shape(dtype, B, S, H, D));
   if (dtype != FA_DTYPE_BF16) return FA_ERR_UNSUPPORTED;
   if (rope == nullptr) return FA_ERR_INVALID_ARG;  // without RoPE call fa_bwd
   FA_TRY(check_rope(rope, D));
@@ -509,7 +509,7 @@ int fa_qk_norm_rope_bwd(int dtype, int B, int T, int I, int H, int D,
 int fa_rope_apply(int dtype, int B, int S, int H, int D, const fa_tensor_t* x,
                   const fa_tensor_t* y, const fa_rope_t* rope, int inverse,
                   void* stream) {
-  FA_TRY(check_shape(dtype, B, S, H, D));
+  FA_TRY(check_attn_shape(dtype, B, S, H, D));
   if (rope == nullptr) return FA_ERR_INVALID_ARG;
   FA_TRY(check_rope(rope, D));
   const int es = dtype == FA_DTYPE_BF16 ? 2 : 4;
@@ -524,7 +524,7 @@ int fa_fwd_partial(int dtype, int B, int S, int kv_len, int H, int D,
                    const fa_tensor_t* q, const fa_tensor_t* k,
                    const fa_tensor_t* v, const fa_tensor_t* o_blk,
                    float* lse_blk, float scale, void* stream) {
-  FA_TRY(check_shape(dtype, B, S, H, D));
+  FA_TRY(check_attn_shape(dtype, B, S, H, D));
   if (kv_len <= 0) return FA_ERR_INVALID_ARG;
   if (!(scale > 0.f) || !std::isfinite(scale)) return FA_ERR_INVALID_ARG;
   const bool bf = dtype == FA_DTYPE_BF16;
@@ -546,7 +546,7 @@ int fa_fwd_fold(int dtype, int B, int S, int kv_len, int H, int D,
                 const fa_tensor_t* q, const fa_tensor_t* k, const fa_tensor_t* v,
                 float* o_acc, float* lse_acc, int step, int last,
                 const fa_tensor_t* o, float* lse, float scale, void* stream) {
-  FA_TRY(check_shape(dtype, B, S, H, D));
+  FA_TRY(check_attn_shape(dtype, B, S, H, D));
   if (dtype != FA_DTYPE_BF16) return FA_ERR_UNSUPPORTED;  // fp32: fa_fwd_partial + fa_lse_merge
   if (kv_len <= 0 || step < 0) return FA_ERR_INVALID_ARG;
   if (!(scale > 0.f) || !std::isfinite(scale)) return FA_ERR_INVALID_ARG;
@@ -570,7 +570,7 @@ int fa_fwd_fold(int dtype, int B, int S, int kv_len, int H, int D,
 int fa_lse_merge(int dtype, int B, int S, int H, int D, float* o_acc,
                  float* lse_acc, const fa_tensor_t* o_blk,
                  const float* lse_blk, int first, void* stream) {
-  FA_TRY(check_shape(dtype, B, S, H, D));
+  FA_TRY(check_attn_shape(dtype, B, S, H, D));
   if (!o_acc || !lse_acc || !lse_blk) return FA_ERR_INVALID_ARG;
   FA_TRY(check_tensor(o_blk, dtype == FA_DTYPE_BF16 ? 2 : 4, false));
   FA_TRY(check_sm100());
@@ -581,7 +581,7 @@ int fa_lse_merge(int dtype, int B, int S, int H, int D, float* o_acc,
 int fa_bwd_prepare(int dtype, int B, int S, int H, int D, const fa_tensor_t* o,
                    const fa_tensor_t* d_o, const float* lse, float* lse2_pad,
                    float* delta_pad, void* stream) {
-  FA_TRY(check_shape(dtype, B, S, H, D));
+  FA_TRY(check_attn_shape(dtype, B, S, H, D));
   const int es = dtype == FA_DTYPE_BF16 ? 2 : 4;
   FA_TRY(check_tensor(o, es, false));
   FA_TRY(check_tensor(d_o, es, false));
@@ -598,7 +598,7 @@ int fa_bwd_partial(int dtype, int B, int S, int kv_len, int H, int D,
                    const float* lse2_pad, const float* delta_pad, float* dq_acc,
                    float* dk_acc, float* dv_acc, int accumulate, float scale,
                    void* stream) {
-  FA_TRY(check_shape(dtype, B, S, H, D));
+  FA_TRY(check_attn_shape(dtype, B, S, H, D));
   if (dtype != FA_DTYPE_BF16) return FA_ERR_UNSUPPORTED;
   if (kv_len <= 0) return FA_ERR_INVALID_ARG;
   if (!(scale > 0.f) || !std::isfinite(scale)) return FA_ERR_INVALID_ARG;
@@ -629,7 +629,7 @@ int fa_add_f32(int64_t n, float* dst, const float* src, void* stream) {
 int fa_cast_f32(int dtype, int B, int S, int H, int D, const float* x,
                 int x_layout, const fa_tensor_t* y, float alpha,
                 const fa_rope_t* rope, void* stream) {
-  FA_TRY(check_shape(dtype, B, S, H, D));
+  FA_TRY(check_attn_shape(dtype, B, S, H, D));
   FA_TRY(check_rope(rope, D));
   if (x == nullptr || (x_layout != 0 && x_layout != 1)) return FA_ERR_INVALID_ARG;
   FA_TRY(check_tensor(y, dtype == FA_DTYPE_BF16 ? 2 : 4, false));
@@ -727,7 +727,7 @@ int fa_bwd_scatter(int dtype, int B, int S, int kv_len, int H, int D, const fa_t
                    const float* lse2_pad, const float* delta_pad, float* dq_acc, int seg,
                    int n_seg, float* const* dk_seg, float* const* dv_seg, float scale,
                    void* stream) {
-  FA_TRY(check_shape(dtype, B, S, H, D));
+  FA_TRY(check_attn_shape(dtype, B, S, H, D));
   if (dtype != FA_DTYPE_BF16) return FA_ERR_UNSUPPORTED;
   if (kv_len <= 0 || seg <= 0 || n_seg < 1 || n_seg > FA_PEER_MAX ||
       (int64_t)seg * n_seg < kv_len || (int64_t)seg * (n_seg - 1) >= kv_len)
@@ -762,7 +762,7 @@ int fa_reduce_cast_f32(int dtype, int B, int S, int H, int D, const float* x, co
                        int n_parts, int64_t part_stride, const fa_tensor_t* y,
                        const fa_tensor_t* y2, float alpha, const fa_rope_t* rope,
                        void* stream) {
-  FA_TRY(check_shape(dtype, B, S, H, D));
+  FA_TRY(check_attn_shape(dtype, B, S, H, D));
   FA_TRY(check_rope(rope, D));
   if (D != 128) return FA_ERR_UNSUPPORTED;
   if (rope != nullptr && (rope->axis_dim != 32 || rope->n_axes != 4)) return FA_ERR_UNSUPPORTED;
@@ -789,7 +789,7 @@ int fa_reduce_cast_f32(int dtype, int B, int S, int H, int D, const float* x, co
 int fa_merge_f32(int dtype, int B, int S, int H, int D, const float* o_a, const float* lse_a,
                  const float* o_b, const float* lse_b, const fa_tensor_t* o, float* lse,
                  void* stream) {
-  FA_TRY(check_shape(dtype, B, S, H, D));
+  FA_TRY(check_attn_shape(dtype, B, S, H, D));
   if (D != 128) return FA_ERR_UNSUPPORTED;
   if (!o_a || !lse_a || !o_b || !lse_b || !lse) return FA_ERR_INVALID_ARG;
   if (reinterpret_cast<uintptr_t>(o_a) % 16 != 0 || reinterpret_cast<uintptr_t>(o_b) % 16 != 0)

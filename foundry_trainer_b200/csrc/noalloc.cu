@@ -16,9 +16,14 @@
 //     call); calls whose work overlaps on the GPU (different streams without
 //     ordering between them) race on the array and give wrong results;
 //   * host code cannot use the array's name as a device address: the address
-//     comes from cudaGetSymbolAddress, taken once per device by the first call
-//     on that device (with that device current), which should therefore come
-//     before any stream capture.
+//     comes from cudaGetSymbolAddress, taken by the first call on a device
+//     (with that device current), which should therefore come before any
+//     stream capture. The address is cached per device together with the
+//     CUDA context it was taken in; after a cudaDeviceReset the next call
+//     sees a new context and looks the address up again.
+#include <cudaTypedefs.h>
+
+#include <cmath>
 #include <mutex>
 
 #include "attn_common.h"
@@ -30,19 +35,39 @@ constexpr size_t kNoAllocScratchBytes = size_t(64) << 20;  // 64 MiB per device
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 static std::mutex g_noalloc_mu;
-static void* g_noalloc_ptr[64];  // device address of the array, per device
+static void* g_noalloc_ptr[64];      // device address of the array, per device
+static CUcontext g_noalloc_ctx[64];  // the context that address belongs to
 
-// Device address of the static scratch on the current device (set up on the
-// first call for that device).
+// The calling thread's current driver context (nullptr when the driver entry
+// point is unavailable; the cached address is then never invalidated).
+static CUcontext current_context() {
+  static PFN_cuCtxGetCurrent_v4000 get = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(fn);
+  });
+  CUcontext ctx = nullptr;
+  if (get != nullptr && get(&ctx) != CUDA_SUCCESS) ctx = nullptr;
+  return ctx;
+}
+
+// Device address of the static scratch on the current device (looked up on
+// the first call for that device, and again when its context was re-created).
 static int noalloc_scratch(void** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return FA_ERR_NO_DEVICE;
+  const CUcontext ctx = current_context();  // nullptr before the runtime made one
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (g_noalloc_ptr[dev] == nullptr) {
+  if (g_noalloc_ptr[dev] == nullptr || g_noalloc_ctx[dev] != ctx) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess) return record_cuda_error(e);
     g_noalloc_ptr[dev] = p;
+    g_noalloc_ctx[dev] = current_context();  // the lookup made the context current
   }
   *out = g_noalloc_ptr[dev];
   return FA_OK;
@@ -60,9 +85,9 @@ extern "C" int fa_bwd_noalloc(int B, int S, int H, int D, const fa_tensor_t* q,
                               const float* lse, const fa_tensor_t* dq,
                               const fa_tensor_t* dk, const fa_tensor_t* dv,
                               float scale, void* stream) {
-  if (B <= 0 || S <= 0 || H <= 0) return FA_ERR_INVALID_ARG;
-  if (D != 128) return FA_ERR_UNSUPPORTED;
-  if (!(scale > 0.f)) return FA_ERR_INVALID_ARG;
+  int rc = check_attn_shape(FA_DTYPE_BF16, B, S, H, D);
+  if (rc != FA_OK) return rc;
+  if (!(scale > 0.f) || !std::isfinite(scale)) return FA_ERR_INVALID_ARG;
   for (const fa_tensor_t* t : {q, k, v, o, d_o, dq, dk, dv}) {
     if (t == nullptr || t->data == nullptr) return FA_ERR_INVALID_ARG;
     if (t->stride_d != 1 || reinterpret_cast<uintptr_t>(t->data) % 16 != 0)
@@ -75,16 +100,17 @@ extern "C" int fa_bwd_noalloc(int B, int S, int H, int D, const fa_tensor_t* q,
       major != 10)
     return FA_ERR_NO_DEVICE;
   // scratch: LSE*log2(e) and Delta padded to 128-row tiles, fp32 dQ accumulator
-  const int s_pad = ((S + 127) / 128) * 128;
-  const size_t rows = (size_t)B * H * s_pad;
+  const int64_t s_pad64 = ((int64_t)S + 127) / 128 * 128;
+  const size_t rows = (size_t)B * (size_t)H * (size_t)s_pad64;
   const size_t need = 2 * round256(rows * 4) + round256(rows * D * 4);
   if (need > kNoAllocScratchBytes) {
     record_error_text("fa_bwd_noalloc: B*H*ceil(S/128)*128 rows need more scratch than the "
                       "64 MiB static array holds; use fa_bwd with a caller workspace");
     return FA_ERR_TOO_LARGE;
   }
+  const int s_pad = (int)s_pad64;  // fits: the rows fit the 64 MiB array
   void* base = nullptr;
-  int rc = noalloc_scratch(&base);
+  rc = noalloc_scratch(&base);
   if (rc != FA_OK) return rc;
   uint8_t* ws = static_cast<uint8_t*>(base);
   float* lse2 = reinterpret_cast<float*>(ws);
@@ -92,10 +118,9 @@ extern "C" int fa_bwd_noalloc(int B, int S, int H, int D, const fa_tensor_t* q,
   float* dq_acc = reinterpret_cast<float*>(ws + 2 * round256(rows * 4));
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const AttnShape sh{B, S, H, D};
-  rc = launch_bwd_delta(FA_DTYPE_BF16, sh, o, d_o, lse, delta, lse2, s_pad, st);
-  if (rc != FA_OK) return rc;
-  // the array keeps the previous call's sums: clear the accumulator
-  rc = record_cuda_error(cudaMemsetAsync(dq_acc, 0, rows * D * 4, st));
+  // the array keeps the previous call's sums: the Delta pass clears the
+  // accumulator on its way
+  rc = launch_bwd_delta(FA_DTYPE_BF16, sh, o, d_o, lse, delta, lse2, s_pad, st, dq_acc);
   if (rc != FA_OK) return rc;
   rc = launch_attn_bwd_bf16(sh, S, q, k, v, d_o, lse2, delta, dq_acc, dk, dv,
                             nullptr, nullptr, 0, scale, nullptr, nullptr, st);

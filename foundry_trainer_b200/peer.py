@@ -184,6 +184,14 @@ class PeerExchange:
             check(lib.fa_copy_2d(dst.data_ptr() + slot * row, self.world * row, src_ptr, row,
                                  row, B, ops._stream_ptr(stream)), "fa_copy_2d")
 
+    def check(self) -> None:
+        """Raises FaError(FA_ERR_DEVICE_TIMEOUT) when a bounded device wait
+        on this device expired since the last check, i.e. a peer did not
+        reach a barrier in time: its shard or its dK/dV contributions are
+        missing and the step's results are wrong. Synchronises the device
+        (and clears the status word)."""
+        check(ops.device_status(), "peer exchange (a peer missed a barrier)")
+
     def close(self) -> None:
         """Unmaps the peers and frees this rank's buffer (all ranks together)."""
         if self._own is None:
@@ -279,6 +287,10 @@ def fold_groups(world: int) -> List[List[int]]:
     return groups
 
 
+def _capturing() -> bool:
+    return torch.cuda.is_available() and torch.cuda.is_current_stream_capturing()
+
+
 def _mark(trace: Optional[list], name: str, stream=None) -> None:
     """Appends (name, timing event recorded on `stream`) when tracing."""
     if trace is not None:
@@ -288,12 +300,15 @@ def _mark(trace: Optional[list], name: str, stream=None) -> None:
 
 
 def peer_fwd(q, k, v, pos, scale, ex: PeerExchange, kern: PeerKernels,
-             trace: Optional[list] = None):
+             trace: Optional[list] = None, check_status: bool = True):
     """(O, LSE, q_rot, k_all, v_all) of this rank's rows; q/k/v (B, S_loc, H, D)
     bf16, pos the shard's (S_loc, 4) positions (None: no RoPE). k_all / v_all
     (B, W*S_loc, H, D) hold the rotated K and the V of every shard, slot t
     (rows [t*S_loc, (t+1)*S_loc)) the shard of rank block_order(rank, W)[t].
-    `trace` (a list) collects device events at the schedule's milestones."""
+    `trace` (a list) collects device events at the schedule's milestones.
+    With `check_status` (and W > 1, outside a CUDA-graph capture) the call ends by
+    synchronising and raising FaError if the barrier's bounded wait expired;
+    a caller that passes False checks `ex.check()` at a point of its own."""
     B, S, H, D = q.shape
     W, r = ex.world, ex.rank
     dev = q.device
@@ -356,12 +371,15 @@ def peer_fwd(q, k, v, pos, scale, ex: PeerExchange, kern: PeerKernels,
     cur.wait_stream(side)
     kern.merge(acc[0][0], acc[0][1], acc[1][0], acc[1][1], o, lse)
     _mark(trace, "merge")
+    if check_status and not _capturing():
+        ex.check()
     return o, lse, q_r, k_all, v_all
 
 
 def peer_bwd(q_r, k_all, v_all, o, d_o, lse, pos, scale, ex: PeerExchange, kern: PeerKernels,
-             trace: Optional[list] = None):
-    """(dq, dk, dv) of this rank's rows w.r.t. the pre-rotation q/k."""
+             trace: Optional[list] = None, check_status: bool = True):
+    """(dq, dk, dv) of this rank's rows w.r.t. the pre-rotation q/k.
+    `check_status` as in peer_fwd (the backward's barrier)."""
     B, S, H, D = q_r.shape
     W = ex.world
     dev = q_r.device
@@ -390,6 +408,8 @@ def peer_bwd(q_r, k_all, v_all, o, d_o, lse, pos, scale, ex: PeerExchange, kern:
     _mark(trace, "reduce")
     kern.cast(dq_acc, 1, scale, pos, dq)
     _mark(trace, "dqcast")
+    if check_status and W > 1 and not _capturing():
+        ex.check()
     return dq, dk, dv
 
 

@@ -2,8 +2,8 @@
  * foundry_attn.h — C ABI of the B200 (sm_100a) joint text+image attention op.
  *
  * This is the drop-in boundary for foundry-trainer's attention custom op
- * `AttnBwd` (crates/foundry-spike/src/lib.rs:151-264). A host binding (the Rust
- * FFI crate described in INTEGRATION.md, the C++ mirror in foundry_attn_op.hpp,
+ * `AttnBwd` (crates/foundry-spike/src/lib.rs:151-264). A host binding (a Rust
+ * FFI crate over these declarations, the C++ mirror in foundry_attn_op.hpp,
  * or the Python ctypes mirror) calls these entry points; nothing here uses
  * torch or any other framework type.
  *
@@ -314,6 +314,9 @@ int fa_merge_f32(int dtype, int B, int S, int H, int D, const float* o_a,
  *     until the process exits.
  *   - The first call on a device looks up the array's device address (with
  *     that device current); make that first call before any stream capture.
+ *     After a cudaDeviceReset the device's context is a new one and the next
+ *     call looks the address up again (so that call, too, belongs outside a
+ *     capture).
  *   - All calls on one device share the array: calls whose GPU work overlaps
  *     (streams without ordering between them) race and corrupt each other's
  *     dQ. The accumulator is cleared at the start of every call.

@@ -4,7 +4,7 @@
 // (crates/foundry-spike/src/lib.rs:151-264) with name() / cpu_fwd / cuda_fwd /
 // bwd, invoked as `q.apply_op3(&k, &v, AttnBwd)` (lib.rs:366, 444). This header
 // keeps that surface in C++ over the C ABI of foundry_attn.h, for hosts that
-// are C++ (and as the shape the Rust binding in INTEGRATION.md follows):
+// are C++ (and as the shape a Rust `impl CustomOp3` over the same C ABI takes):
 //   * storages are owned by the caller's allocator, as Candle owns them; the op
 //     returns freshly allocated outputs (lib.rs:185, 212);
 //   * errors are values (Result), like candle_core::Result / bail!;

@@ -63,6 +63,10 @@ class ThreadPeers:
                 torch.cuda.synchronize()
                 peers.barrier_.wait()
 
+            def check(self):
+                from foundry_trainer_b200 import _lib, ops
+                _lib.check(ops.device_status(), "thread peers")
+
             def pull(self, par, src, slot, which, dst, stream):
                 from foundry_trainer_b200 import _lib, ops
                 B, S, H, D = peers.shape
@@ -151,6 +155,7 @@ class GlooExchange:
         self._recv = [torch.zeros((self.world, 2) + self.shape) for _ in range(2)]
         self._gathered = [None, None]
         self.outbox = {}
+        self.status = 0  # what the device status word would hold
 
     def pub(self, par):
         return tuple(self._pub[par])
@@ -162,22 +167,41 @@ class GlooExchange:
         return [(par, owner, self.rank, which) for owner in range(self.world)]
 
     def barrier(self, channel, stream=None):
+        """The device barrier's stand-in. Like the device kernel, a barrier
+        that cannot complete (a peer left: the gloo collective fails or runs
+        into the group's timeout) records FA_ERR_DEVICE_TIMEOUT and returns;
+        the data a missing peer would have delivered stays stale (zeros),
+        and `check()` raises."""
         dist, W = self.dist, self.world
         if channel == 0:
             par = (self.n_fwd - 1) % 2
             mine = torch.stack(self._pub[par])
             got = [torch.empty_like(mine) for _ in range(W)]
-            dist.all_gather(got, mine)
+            try:
+                dist.all_gather(got, mine)
+                dist.barrier()
+            except RuntimeError:
+                self.status = 5  # FA_ERR_DEVICE_TIMEOUT
+                got = [mine if r == self.rank else torch.zeros_like(mine) for r in range(W)]
             self._gathered[par] = got
         else:
             par = (self.n_bwd - 1) % 2
             mine = torch.stack([torch.stack([self.outbox[(par, o, self.rank, w)] for w in (0, 1)])
                                 for o in range(W)])  # (owner, which, B, S, H, D)
             got = [torch.empty_like(mine) for _ in range(W)]
-            dist.all_gather(got, mine)
+            try:
+                dist.all_gather(got, mine)
+                dist.barrier()
+            except RuntimeError:
+                self.status = 5
+                return
             for src in range(W):
                 self._recv[par][src] = got[src][self.rank]
-        dist.barrier()
+
+    def check(self):
+        from foundry_trainer_b200 import _lib
+        status, self.status = self.status, 0
+        _lib.check(status, "gloo peers")
 
     def pull(self, par, src, slot, which, dst, stream):
         S = self.shape[1]
@@ -255,5 +279,50 @@ def peer_gloo_rank(rank, world, port, shape, seed, results, steps=2):
             o, lse, q_r, k_all, v_all = peer.peer_fwd(qs, ks, vs, ps, scale, ex, kern)
             dq, dk, dv = peer.peer_bwd(q_r, k_all, v_all, o, dos, lse, ps, scale, ex, kern)
         results.put((rank, o.numpy(), dq.numpy(), dk.numpy(), dv.numpy(), kern.calls))
+    finally:
+        dist.destroy_process_group()
+
+
+def peer_gloo_rank_leaves(rank, world, port, shape, seed, results, leave_after=1,
+                          timeout_s=10.0):
+    """Failure detection on gloo ranks: every rank runs the peer schedule;
+    the last rank leaves after `leave_after` fwd+bwd steps (between steps,
+    nothing of its own in flight), the others go on to the next step. A
+    survivor's barrier cannot complete, records the timeout status, and the
+    step's status check raises FaError instead of hanging. Reports (rank,
+    steps completed, status code of the raised error or 0, seconds)."""
+    import time
+
+    import torch.distributed as dist
+
+    from foundry_trainer_b200 import _lib, ops, peer
+    from tests.ring_support import full_problem
+
+    torch.cuda.current_stream = lambda *a, **k: _NoStream()
+    torch.cuda.Event = _NoEvent
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=timeout_s))
+    done, code, t0 = 0, 0, time.time()
+    try:
+        B, S, H, D = shape
+        q, k, v, d_o, pos = full_problem(B, S, H, D, seed)
+        n = S // world
+        sl = slice(rank * n, (rank + 1) * n)
+        qs, ks, vs, dos = (t[:, sl].contiguous() for t in (q, k, v, d_o))
+        ps = pos[sl].contiguous()
+        ex = GlooExchange((B, n, H, D))
+        kern = fake_peer_kernels(ex)
+        scale = ops.default_scale(D)
+        steps = leave_after if rank == world - 1 else leave_after + 1
+        try:
+            for _ in range(steps):
+                o, lse, q_r, k_all, v_all = peer.peer_fwd(qs, ks, vs, ps, scale, ex, kern)
+                peer.peer_bwd(q_r, k_all, v_all, o, dos, lse, ps, scale, ex, kern)
+                done += 1
+        except _lib.FaError as e:
+            code = e.status
+        results.put((rank, done, code, time.time() - t0))
     finally:
         dist.destroy_process_group()

@@ -38,3 +38,26 @@ def test_block_cpu_baseline_sample_runs_small():
     import bench
     steps_per_s, secs = bench.cpu_block_sample(txt_len=8, grid=4, dim=256, heads=2, rank_lora=4)
     assert steps_per_s > 0 and secs > 0
+
+
+def test_reference_arm_row_sample_counts_its_flops():
+    sys.path.insert(0, str(ROOT))
+    import numpy as np
+
+    import bench
+    from foundry_trainer_b200 import configs
+    from oracle import attn_oracle as orc
+    pos = configs.positions(8, 4).numpy()  # S = 24
+    g = np.random.default_rng(0)
+    qn, kn, vn, dn = (g.standard_normal((24, 1, 128)).astype(np.float32) for _ in range(4))
+    assert bench._oracle_rows_step(orc, qn, kn, vn, dn, pos, 6) == 14.0 * 6 * 24 * 128
+
+
+def test_reference_arm_other_ranks_exit_quietly():
+    import os
+    env = dict(os.environ, RANK="1", WORLD_SIZE="2", LOCAL_RANK="1")
+    out = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference",
+                          "--steps", "1", "--warmup", "1"], capture_output=True, text=True,
+                         timeout=600, cwd=ROOT, env=env)
+    assert out.returncode == 0, out.stderr[-2000:]
+    assert not [ln for ln in out.stdout.splitlines() if ln.startswith("{")]

@@ -220,3 +220,25 @@ def test_data_parallel_lora_replicas_on_gloo_match_averaged_gradients():
             assert bs.rel_l2(got[r][0][i], mean[i]) <= 1e-5, (r, k)
     assert all(torch.equal(got[0][1][k], got[1][1][k]) for k in tr.keys)
     assert any(not torch.equal(got[0][1][k], p.detach()) for k, p in zip(tr.keys, tr.params))
+
+
+def test_kept_attention_values_are_reused_only_for_the_same_inputs():
+    # the guard of the checkpointed attention callables (attn.kept_key /
+    # kept_matches): equal inputs in fresh tensors match (the checkpointed
+    # recompute); another shape, another weight version, or a changed
+    # sampled row do not (a stale kept O/LSE is never reused)
+    from foundry_trainer_b200 import attn
+    g = torch.Generator().manual_seed(4)
+    xs = [torch.randn(1, 300, 2, 128, generator=g) for _ in range(3)]
+    ws = [torch.rand(128, generator=g) for _ in range(2)]
+    key = attn.kept_key(xs, ws)
+    assert attn.kept_matches(key, [x.clone() for x in xs], ws)
+    assert not attn.kept_matches(None, xs, ws)
+    assert not attn.kept_matches(key, [xs[0][:, :299]] + xs[1:], ws)
+    assert not attn.kept_matches(key, xs, [ws[0].clone(), ws[1]])  # another weight tensor
+    ws[1].mul_(1.0)  # same values, new version: the weights may have been updated
+    assert not attn.kept_matches(key, xs, ws)
+    key = attn.kept_key(xs, ws)
+    changed = [x.clone() for x in xs]
+    changed[2][0, 0, 1, 5] += 1.0  # row 0 is sampled
+    assert not attn.kept_matches(key, changed, ws)

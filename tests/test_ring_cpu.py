@@ -138,3 +138,37 @@ def test_peer_schedule_matches_single_sequence_oracle(world, S):
         assert orc.max_rel(ours, ref) <= TOL, (name, orc.max_rel(ours, ref))
     calls = shards[0][4]
     assert calls.count("merge") == 2 and calls.count("reduce_cast") == 2  # two steps
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_peer_schedule_survivors_raise_timeout_when_a_rank_leaves(world):
+    # failure detection (no GPU): the last rank leaves between steps; the
+    # survivors' next barrier cannot complete, records FA_ERR_DEVICE_TIMEOUT
+    # like the device barrier's bounded wait, and peer_fwd's status check
+    # raises instead of the step returning wrong results or hanging
+    from tests import peer_support
+    ctx = mp.get_context("spawn")
+    results = ctx.Queue()
+    port = _free_port()
+    shape = (1, 24 * world, 2, 128)
+    procs = [ctx.Process(target=peer_support.peer_gloo_rank_leaves,
+                         args=(r, world, port, shape, 3, results, 1, 10.0))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    got = {}
+    try:
+        for _ in range(world):
+            r, done, code, secs = results.get(timeout=120)
+            got[r] = (done, code, secs)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert got[world - 1][:2] == (1, 0)  # the leaver finished its one step cleanly
+    for r in range(world - 1):
+        done, code, secs = got[r]
+        assert done == 1 and code == 5, (r, got[r])  # FA_ERR_DEVICE_TIMEOUT on step 2
+        assert secs < 90, (r, secs)

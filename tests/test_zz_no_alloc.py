@@ -51,11 +51,15 @@ def test_noalloc_backward_matches_workspace_backward_twice():
     o, lse = ops.attn_fwd(q, k, v)
     ref = ops.attn_bwd(q, k, v, o, d_o, lse)
     torch.cuda.synchronize()
+    f = lambda t: t.float().cpu().numpy()
+    _, _, odq, odk, odv = orc.attn_fwd_bwd_bshd(f(q), f(k), f(v), f(d_o), "f32")
     for call in range(2):
         got = _noalloc(lib, q, k, v, o, d_o, lse, scale)
-        for name, a, b in zip(("dq", "dk", "dv"), got, ref):
-            err = orc.max_rel(a.float().cpu().numpy(), b.float().cpu().numpy())
-            assert err <= TOL, (call, name, err)
+        for name, a, b, r in zip(("dq", "dk", "dv"), got, ref, (odq, odk, odv)):
+            err = orc.max_rel(f(a), f(b))
+            assert err <= TOL, (call, name, "vs fa_bwd", err)
+            err = orc.max_rel(f(a), r)
+            assert err <= TOL, (call, name, "vs oracle", err)
     assert ops.device_status() == 0
 
 
@@ -71,3 +75,23 @@ def test_noalloc_refuses_sizes_beyond_its_array():
                             *[C.byref(d)] * 3, 0.088, None)
     assert rc == _lib.FA_ERR_TOO_LARGE
     assert b"64 MiB" in lib.fa_last_error()
+
+
+def test_noalloc_refuses_what_fa_bwd_refuses():
+    import math
+
+    from foundry_trainer_b200 import _lib
+    from foundry_trainer_b200.ops import desc
+    lib = _lib.load()
+    t = torch.empty((1, 16, 1, 128), device="cuda", dtype=torch.bfloat16)
+    d = desc(t)
+    lse = torch.empty(16, device="cuda")
+    call = lambda B, S, H, D, scale: lib.fa_bwd_noalloc(B, S, H, D, *[C.byref(d)] * 5,
+                                                        lse.data_ptr(), *[C.byref(d)] * 3,
+                                                        scale, None)
+    for scale in (math.inf, math.nan, 0.0, -1.0):
+        assert call(1, 16, 1, 128, scale) == _lib.FA_ERR_INVALID_ARG, scale
+    assert call(1, 16, 1, 64, 0.088) == _lib.FA_ERR_UNSUPPORTED
+    assert call(0, 16, 1, 128, 0.088) == _lib.FA_ERR_INVALID_ARG
+    # the row padding is computed without int overflow: refused as too large
+    assert call(1, 2**31 - 1, 1, 128, 0.088) == _lib.FA_ERR_TOO_LARGE
