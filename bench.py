@@ -709,6 +709,46 @@ def main():
                 "bwd_kernel_ms": bwd_ms,
                 "flops_per_launch": bwd_flops}
 
+    # ---- secondary: the same step with the deterministic backward
+    # (fa_bwd deterministic=1: identical bits across repeats), same timing
+    det = None
+    if not ring_mode:
+        o_d, lse_d = torch.empty_like(q), torch.empty((q.shape[0], cfg.H, cfg.S), device=dev)
+        dq_d, dk_d, dv_d = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+
+        def det_step():
+            ops.attn_fwd(q, k, v, rope=rope, out=o_d, lse=lse_d)
+            ops.attn_bwd(q, k, v, o_d, d_o, lse_d, rope=rope, dq=dq_d, dk=dk_d, dv=dv_d,
+                         deterministic=True)
+        for _ in range(args.warmup):
+            det_step()
+        g_det = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_det):
+            det_step()
+        g_det.replay()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ds_, de_ = ([torch.cuda.Event(enable_timing=True) for _ in range(K)] for _ in range(2))
+        for i in range(K):
+            flush_buf.zero_()
+            ds_[i].record()
+            g_det.replay()
+            de_[i].record()
+        torch.cuda.synchronize()
+        td = torch.tensor([sum(a.elapsed_time(b) for a, b in zip(ds_, de_))], device=dev,
+                          dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(td, op=dist.ReduceOp.MAX)
+        det = {"value": K * flops_step / (td.item() / 1e3) / 1e12, "unit": UNIT,
+               "ms_per_step": td.item() / K,
+               "what": "the same step with fa_bwd deterministic=1 (bit-identical repeats: each "
+                       "128-key tile's dQ contribution stored in its own fp32 slot, summed in "
+                       "slot order by the finish pass; no fa_bwd_saved reuse)"}
+        del g_det
+        if ops.device_status() != 0:
+            raise RuntimeError("device-side bounded wait expired (deterministic step)")
+
     # ---- end to end through the public API with host buffers
     e2e = None
     if not args.no_e2e:
@@ -853,6 +893,7 @@ def main():
         "gpu_launches": launches_per_step * K,
         "clocks": clocks,
         "wall_s_timed": wall,
+        "deterministic": det,
     }
     print(json.dumps(line), flush=True)
 

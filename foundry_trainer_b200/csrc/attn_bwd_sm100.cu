@@ -23,8 +23,9 @@
 //   warps 4-7     dQ drain: dQ^T from TMEM, staged row-major (query, d) in
 //                 the step's own Q_i|dO_i slot (64 KB, free once the dQ^T MMA
 //                 has completed), added into dq_acc (B, H, S_pad, D) with TMA
-//                 bulk reduce-adds (fp32); the slot goes back to the producer
-//                 when the reduces have read it
+//                 bulk reduce-adds (fp32) — or, in deterministic mode, stored
+//                 to this CTA's own partial slot with bulk copies; the slot
+//                 goes back to the producer when the bulk ops have read it
 // TMEM (512 columns):
 //   A [0,128)    S^T_i; after the softmax, per query half h (columns
 //                64h..64h+63): P^T (bf16 pairs, 32 columns) then dS^T (32
@@ -101,6 +102,11 @@ struct Params {
   float* dk_acc;            // (B, kv_len, H, D) fp32
   float* dv_acc;
   float* dq_acc;            // (B, H, s_pad, D) fp32, zeroed by the caller
+  // Deterministic mode (dq_acc unused): the CTA of K/V tile t stores its
+  // contribution to each dQ tile into its own slot t of the fp32
+  // (n_kv_tiles, B, H, s_pad, D) array; a later pass sums the slots in index
+  // order, so repeated runs give the same bits. nullptr: reduce-adds.
+  float* dq_part;
   RopeArgs rope;            // rope.pos == nullptr: no rotation
 };
 
@@ -118,6 +124,13 @@ __device__ __forceinline__ void bulk_reduce_add_f32(float* dst, const float* src
           dst),
       "r"(smem_u32(src)), "r"(bytes)
       : "memory");
+}
+
+// dst[0 .. bytes/4) = src[...], performed by the TMA unit.
+__device__ __forceinline__ void bulk_store_f32(float* dst, const float* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
+               "r"(smem_u32(src)), "r"(bytes)
+               : "memory");
 }
 
 __device__ __forceinline__ void bulk_load(void* dst, const void* src,
@@ -380,6 +393,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
     const uint32_t t_a = tmem + lane_off + kColA + (uint32_t)half * 64u;
     const uint32_t t_b = tmem + lane_off + kColB + (uint32_t)half * 64u;
     const float sl2 = p.scale_log2;
+    const uint64_t sl2_2 = f2_pack(sl2, sl2);
     bool ok = true;
     for (int i = 0; i < nq; ++i) {
       const int st = i & 1, n = i >> 1;
@@ -407,22 +421,32 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
         tmem_wait_ld();
         const uint32_t* sr = cb < 2 ? s_lo : s_hi + (cb - 2) * 16;
         uint32_t pk[8], dk[8];
+        // pairs of columns through the packed fp32x2 pipe (each lane rounds
+        // as the scalar instruction would): x = S*scale*log2e - LSE2,
+        // P = 2^x, dS = P * (dP - Delta)
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const float4 l = lse4[cb * 4 + u];
           const float4 dl = dlt4[cb * 4 + u];
           const int c = 4 * u;
-          const int e = 4 * u;
-          const float p0 = fast_exp2(fmaf(__uint_as_float(sr[c + 0]), sl2, -l.x));
-          const float p1 = fast_exp2(fmaf(__uint_as_float(sr[c + 1]), sl2, -l.y));
-          const float p2 = fast_exp2(fmaf(__uint_as_float(sr[c + 2]), sl2, -l.z));
-          const float p3 = fast_exp2(fmaf(__uint_as_float(sr[c + 3]), sl2, -l.w));
+          float x0, x1, x2, x3;
+          f2_unpack(ffma2(f2_pack(__uint_as_float(sr[c + 0]), __uint_as_float(sr[c + 1])),
+                          sl2_2, f2_pack(-l.x, -l.y)), x0, x1);
+          f2_unpack(ffma2(f2_pack(__uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3])),
+                          sl2_2, f2_pack(-l.z, -l.w)), x2, x3);
+          const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
+          const float p2 = fast_exp2(x2), p3 = fast_exp2(x3);
           pk[2 * u] = pack_bf16(p0, p1);
           pk[2 * u + 1] = pack_bf16(p2, p3);
-          dk[2 * u] = pack_bf16(p0 * (__uint_as_float(dr[e + 0]) - dl.x),
-                                p1 * (__uint_as_float(dr[e + 1]) - dl.y));
-          dk[2 * u + 1] = pack_bf16(p2 * (__uint_as_float(dr[e + 2]) - dl.z),
-                                    p3 * (__uint_as_float(dr[e + 3]) - dl.w));
+          float d0, d1, d2, d3;
+          f2_unpack(fmul2(f2_pack(p0, p1),
+                          fsub2(f2_pack(__uint_as_float(dr[c + 0]), __uint_as_float(dr[c + 1])),
+                                f2_pack(dl.x, dl.y))), d0, d1);
+          f2_unpack(fmul2(f2_pack(p2, p3),
+                          fsub2(f2_pack(__uint_as_float(dr[c + 2]), __uint_as_float(dr[c + 3])),
+                                f2_pack(dl.z, dl.w))), d2, d3);
+          dk[2 * u] = pack_bf16(d0, d1);
+          dk[2 * u + 1] = pack_bf16(d2, d3);
         }
         tmem_st8(t_a + cb * 8, pk);       // P^T: columns 64h + [0, 32)
         tmem_st8(t_a + 32 + cb * 8, dk);  // dS^T: columns 64h + [32, 64)
@@ -480,7 +504,10 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
     const uint32_t lane_off = (uint32_t)(sub * 32) << 16;
     const uint32_t t_b = tmem + lane_off + kColB;
     const bool leader = (warp == 4 && lane == 0);
-    float* dq_bh = p.dq_acc + ((int64_t)b * p.H + h) * p.s_pad * 128;
+    const int64_t bh_rows = ((int64_t)b * p.H + h) * p.s_pad;
+    float* dq_bh = p.dq_part != nullptr
+                       ? p.dq_part + ((int64_t)kv_tile * gridDim.z * p.H * p.s_pad + bh_rows) * 128
+                       : p.dq_acc + bh_rows * 128;
     // a thread writes column d of 64 query rows; a warp 128 contiguous bytes
     auto stage = [&](float* buf, const uint32_t* v) {
 #pragma unroll
@@ -546,8 +573,13 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
       fence_proxy_async_smem();
       named_bar_sync(2, 128);
       if (leader) {
-        bulk_reduce_add_f32(dst, buf, 32768);
-        bulk_reduce_add_f32(dst + 64 * 128, buf + 64 * 128, 32768);
+        if (p.dq_part != nullptr) {
+          bulk_store_f32(dst, buf, 32768);
+          bulk_store_f32(dst + 64 * 128, buf + 64 * 128, 32768);
+        } else {
+          bulk_reduce_add_f32(dst, buf, 32768);
+          bulk_reduce_add_f32(dst + 64 * 128, buf + 64 * 128, 32768);
+        }
         bulk_commit_group();
         reduce_pending = st;  // slot handed back once the reduces have read it
       }
@@ -577,7 +609,7 @@ int launch_attn_bwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
                          const fa_tensor_t* dk, const fa_tensor_t* dv,
                          float* dk_acc, float* dv_acc, int accumulate, float scale,
                          const fa_rope_t* rope, const float2* rope_table,
-                         cudaStream_t stream, const BwdScatter* scatter) {
+                         cudaStream_t stream, const BwdScatter* scatter, float* dq_part) {
   if (rope != nullptr && (rope->axis_dim != 32 || rope->n_axes != 4))
     return FA_ERR_UNSUPPORTED;  // the dK epilogue un-rotates 32-wide axes
   if (rope != nullptr && rope_table == nullptr)
@@ -620,6 +652,7 @@ int launch_attn_bwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
   p.dk_acc = dk_acc;
   p.dv_acc = dv_acc;
   p.dq_acc = dq_acc;
+  p.dq_part = dq_part;
   p.rope = make_rope_args(rope);
   p.rope.table = rope_table;
   rc = ensure_smem_attr((const void*)bwd::attn_bwd_kernel, bwd::kSmemBytes,

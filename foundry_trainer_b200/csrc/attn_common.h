@@ -72,7 +72,8 @@ int launch_attn_bwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
                          const fa_tensor_t* dk, const fa_tensor_t* dv,
                          float* dk_acc, float* dv_acc, int accumulate, float scale,
                          const fa_rope_t* rope, const float2* rope_table,
-                         cudaStream_t stream, const BwdScatter* scatter = nullptr);
+                         cudaStream_t stream, const BwdScatter* scatter = nullptr,
+                         float* dq_part = nullptr);
 
 // fp32 SIMT kernels (exact path)
 int launch_attn_fwd_f32(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
@@ -113,6 +114,12 @@ int launch_cast_f32(int dtype, const AttnShape& sh, const float* x,
                     const fa_tensor_t* y, float alpha, const fa_rope_t* rope,
                     int pos_offset, cudaStream_t stream, const float2* table = nullptr,
                     int s_pad = 0);
+// dQ of the deterministic bf16 backward: y = alpha * inverse_rope(sum over
+// j < n_parts of x[j]) in index order; x fp32 (n_parts, B, H, s_pad, D),
+// parts part_stride floats apart (rope may be nullptr; table as above)
+int launch_dq_parts_finish(int dtype, const AttnShape& sh, const float* x, int n_parts,
+                           int64_t part_stride, int s_pad, const fa_tensor_t* y, float alpha,
+                           const fa_rope_t* rope, const float2* table, cudaStream_t stream);
 // dst[i] += src[i], i < n
 int launch_add_f32(int64_t n, float* dst, const float* src, cudaStream_t stream);
 int launch_lse_merge(int dtype, const AttnShape& sh, float* o_acc,

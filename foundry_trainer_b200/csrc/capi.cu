@@ -306,17 +306,19 @@ int fa_fwd(int dtype, int B, int S, int H, int D, const fa_tensor_t* q,
 }
 
 // workspace: [q_rot | k_rot] (rope) | lse2_pad | delta_pad | dq_acc (bf16) ;
+//            deterministic bf16: dq_acc replaced by the per-K/V-tile dQ
+//            partials (n_kv_tiles, B, H, S_pad, D) ;
 //            [q_rot | k_rot | dq_rot | dk_rot] (rope) | delta (f32)
 size_t fa_bwd_workspace_bytes(int dtype, int B, int S, int H, int D,
                               const fa_rope_t* rope, int deterministic) {
-  (void)deterministic;
   const size_t n = (size_t)B * S * H * D;
   if (dtype == FA_DTYPE_BF16) {
     const size_t s_pad = (size_t)((S + 127) / 128) * 128;
     size_t total = rope_table_bytes(S, rope);
     if (rope) total += 2 * align256(n * 2);
     total += 2 * align256((size_t)B * H * s_pad * 4);
-    total += align256((size_t)B * H * s_pad * D * 4);  // dq_acc (B, H, S_pad, D)
+    const size_t acc = (size_t)B * H * s_pad * D * 4;  // one (B, H, S_pad, D) fp32 array
+    total += align256(deterministic ? (s_pad / 128) * acc : acc);
     return total;
   }
   size_t total = rope_table_bytes(S, rope);
@@ -339,7 +341,6 @@ int fa_bwd(int dtype, int B, int S, int H, int D, const fa_tensor_t* q,
   for (const fa_tensor_t* t : {q, k, v, d_o}) FA_TRY(check_tensor(t, es, bf));
   for (const fa_tensor_t* t : {o, dq, dk, dv}) FA_TRY(check_tensor(t, es, true));
   if (lse == nullptr) return FA_ERR_INVALID_ARG;
-  if (bf && deterministic) return FA_ERR_UNSUPPORTED;
   FA_TRY(check_sm100());
   const size_t need = fa_bwd_workspace_bytes(dtype, B, S, H, D, rope, deterministic);
   if (workspace == nullptr || workspace_bytes < need) return FA_ERR_WORKSPACE;
@@ -369,6 +370,20 @@ int fa_bwd(int dtype, int B, int S, int H, int D, const fa_tensor_t* q,
     float* delta = reinterpret_cast<float*>(ws);
     ws += align256((size_t)B * H * s_pad * 4);
     float* dq_acc = reinterpret_cast<float*>(ws);
+    if (deterministic) {
+      // every K/V tile's dQ contribution lands in its own slot (plain
+      // stores, nothing to clear), summed in slot order by the finish pass
+      FA_TRY(launch_bwd_delta(dtype, sh, o, d_o, lse, delta, lse2, s_pad, st));
+      cudaEvent_t stop = timer_begin(FA_TIMER_BWD, st);
+      const int rc = launch_attn_bwd_bf16(sh, S, &qr, &kr, v, d_o, lse2, delta, nullptr, dk, dv,
+                                          nullptr, nullptr, 0, scale, rope, table, st, nullptr,
+                                          dq_acc);
+      timer_end(stop, st);
+      FA_TRY(rc);
+      return launch_dq_parts_finish(dtype, sh, dq_acc, s_pad / 128,
+                                    (int64_t)B * H * s_pad * D, s_pad, dq, scale, rope, table,
+                                    st);
+    }
     // Delta / LSE2 prologue; it also clears the dQ accumulator
     FA_TRY(launch_bwd_delta(dtype, sh, o, d_o, lse, delta, lse2, s_pad, st, dq_acc));
     cudaEvent_t stop = timer_begin(FA_TIMER_BWD, st);

@@ -217,6 +217,66 @@ rope_token_kernel(TView x0, TOut y0, TView x1, TOut y1,
   }
 }
 
+// dQ finish of the deterministic backward: y[b, s, h] = alpha *
+// inverse_rope(x[0] + x[1] + ... + x[n_parts-1]) for the (b, h, s) row of
+// the fp32 (n_parts, B, H, s_pad, 128) partials, summed left to right in
+// slot order (so the same inputs give the same bits). One block per token
+// (b, s); warp w handles heads w, w+4, ...; lane l owns elements 4l..4l+3
+// and keeps eight slots' loads in flight.
+__global__ void __launch_bounds__(32 * kRopeWarps)
+dq_parts_finish_kernel(const float* x, int n_parts, int64_t part_stride, TOut y,
+                       const __grid_constant__ RopeArgs r, int S, int H, int s_pad,
+                       float alpha, int out_bf16) {
+  __shared__ float2 cs_s[64];
+  const int s = (int)(blockIdx.x % S), b = (int)(blockIdx.x / S);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool rotate = r.pos != nullptr;
+  if (rotate && threadIdx.x < 64) {
+    const int64_t ti = (int64_t)(s + r.pos_offset) * 64 + threadIdx.x;
+    cs_s[threadIdx.x] = r.table != nullptr ? r.table[ti] : rope_cs_direct(r, s, threadIdx.x);
+  }
+  __syncthreads();
+  // inverse rotation: first half x c + x' s, second half x c - x' s
+  const float sgn = (lane & 7) < 4 ? 1.f : -1.f;
+  const int f0 = (lane >> 3) * 16 + (lane & 3) * 4;
+  constexpr int kBatch = 8;
+  for (int h = warp; h < H; h += kRopeWarps) {
+    const float* src = x + (((int64_t)b * H + h) * s_pad + s) * 128 + 4 * lane;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int j0 = 0; j0 < n_parts; j0 += kBatch) {
+      float4 t[kBatch];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u)
+        if (j0 + u < n_parts)
+          t[u] = __ldcs(reinterpret_cast<const float4*>(src + (int64_t)(j0 + u) * part_stride));
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u)
+        if (j0 + u < n_parts) {
+          v[0] += t[u].x;
+          v[1] += t[u].y;
+          v[2] += t[u].z;
+          v[3] += t[u].w;
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) v[u] *= alpha;
+    if (rotate) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float other = __shfl_xor_sync(0xffffffffu, v[u], 4);
+        const float2 cs = cs_s[f0 + u];
+        v[u] = __fadd_rn(__fmul_rn(v[u], cs.x), __fmul_rn(sgn * other, cs.y));
+      }
+    }
+    if (out_bf16)
+      Vec4<__nv_bfloat16>::store(reinterpret_cast<__nv_bfloat16*>(y.p) + b * y.sb + s * y.ss +
+                                     h * y.sh + 4 * lane, v);
+    else
+      Vec4<float>::store(reinterpret_cast<float*>(y.p) + b * y.sb + s * y.ss + h * y.sh + 4 * lane,
+                         v);
+  }
+}
+
 // bf16 -> bf16 rotation for the reference layout, eight tokens per block:
 // lane l of a half-warp owns elements 8l..8l+7 of a row (one 16-byte access;
 // the rotate-half partner of element 8l+u is element 8(l^2)+u), so a warp
@@ -663,6 +723,24 @@ int launch_cast_f32(int dtype, const AttnShape& sh, const float* x,
                 : misc::TView{x, (int64_t)sh.S * sh.H * D, (int64_t)sh.H * D, D};
   return launch_rope_generic(FA_DTYPE_F32, dtype, sh, xv, misc::tout(y), r,
                              alpha, 1, stream);
+}
+
+int launch_dq_parts_finish(int dtype, const AttnShape& sh, const float* x, int n_parts,
+                           int64_t part_stride, int s_pad, const fa_tensor_t* y, float alpha,
+                           const fa_rope_t* rope, const float2* table, cudaStream_t stream) {
+  if (sh.D != 128 || n_parts <= 0) return FA_ERR_UNSUPPORTED;
+  if (rope != nullptr && (rope->axis_dim != 32 || rope->n_axes != 4)) return FA_ERR_UNSUPPORTED;
+  const misc::TOut yo = misc::tout(y);
+  const int es = dtype == FA_DTYPE_BF16 ? 2 : 4;
+  if (reinterpret_cast<uintptr_t>(yo.p) % (4 * es) != 0 || (yo.sb * es) % (4 * es) != 0 ||
+      (yo.ss * es) % (4 * es) != 0 || (yo.sh * es) % (4 * es) != 0)
+    return FA_ERR_ALIGNMENT;
+  RopeArgs r = make_rope_args(rope, dtype == FA_DTYPE_BF16 ? 1 : 0, 0);
+  r.table = table;
+  const dim3 grid((unsigned)((int64_t)sh.B * sh.S));
+  misc::dq_parts_finish_kernel<<<grid, 32 * misc::kRopeWarps, 0, stream>>>(
+      x, n_parts, part_stride, yo, r, sh.S, sh.H, s_pad, alpha, dtype == FA_DTYPE_BF16);
+  return launch_status();
 }
 
 int launch_add_f32(int64_t n, float* dst, const float* src, cudaStream_t stream) {

@@ -99,10 +99,15 @@ size_t fa_fwd_workspace_bytes(int dtype, int B, int S, int H, int D,
  * forward output o, its gradient d_o and the saved lse, writes dq, dk, dv
  * (w.r.t. the pre-rotation q/k when `rope` is non-NULL).
  * `deterministic` != 0 requests bit-identical results across repeats
- * (the reference's stability gate, bin/stability.rs:175-190); the f32 path is
- * always deterministic.
+ * (the reference's stability gate, bin/stability.rs:177-189: identical bits
+ * across repeat runs, docs/TESTING.md:19); the f32 path is always
+ * deterministic. The bf16 path then stores each 128-key tile's dQ
+ * contribution in its own fp32 slot and sums the slots in a fixed order
+ * instead of adding them into one accumulator in arrival order: its
+ * workspace grows to B*H*ceil(S/128)*S_pad*D*4 bytes (S_pad = S rounded up
+ * to 128; 2 GB at B1 H24 S4608) and the sum is one extra pass over it.
  * `workspace` must hold fa_bwd_workspace_bytes(); it carries the fp32 dQ
- * accumulator and the per-row softmax-gradient term.
+ * accumulator (or the partials) and the per-row softmax-gradient term.
  */
 int fa_bwd(int dtype, int B, int S, int H, int D,
            const fa_tensor_t* q, const fa_tensor_t* k, const fa_tensor_t* v,

@@ -175,3 +175,34 @@ def test_bf16_op_mirror_with_rope_under_autograd():
                                                  rope_pos=pos.numpy())
     assert_close({"o": np32(out), "dq": np32(q.grad), "dk": np32(k.grad), "dv": np32(v.grad)},
                  {"o": ro, "dq": rdq, "dk": rdk, "dv": rdv}, TOL, "op3 rope")
+
+
+@pytest.mark.parametrize("B,S,H,with_rope", [(2, 700, 3, False), (1, 680, 2, True),
+                                             (1, 130, 1, True)])
+def test_bf16_deterministic_backward_repeats_bit_identical(B, S, H, with_rope):
+    """deterministic=1: three repeats give identical bits (the reference's
+    gate, docs/TESTING.md:19 and bin/stability.rs:177-189), and the result
+    is the op's gradient (oracle, 2e-2)."""
+    from foundry_trainer_b200 import configs, ops
+    g = torch.Generator().manual_seed(31 + S)
+    shape = (B, S, H, 128)
+    q, k, v = ((torch.randn(shape, generator=g) * 0.5).to(torch.bfloat16).cuda() for _ in range(3))
+    d_o = torch.randn(shape, generator=g).to(torch.bfloat16).cuda()
+    pos = None
+    rope = None
+    if with_rope:
+        pos = torch.zeros((S, 4))
+        pos[:, 1] = torch.arange(S).float() // 24
+        pos[:, 2] = torch.arange(S).float() % 24
+        rope = ops.Rope(pos.cuda())
+    o, lse = ops.attn_fwd(q, k, v, rope=rope)
+    runs = [ops.attn_bwd(q, k, v, o, d_o, lse, rope=rope, deterministic=True) for _ in range(3)]
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    for rep in runs[1:]:
+        for name, a, b in zip(("dq", "dk", "dv"), runs[0], rep):
+            assert torch.equal(a, b), name
+    _, _, rdq, rdk, rdv = orc.attn_fwd_bwd_bshd(np32(q), np32(k), np32(v), np32(d_o), "f32",
+                                                rope_pos=pos.numpy() if pos is not None else None)
+    assert_close({"dq": np32(runs[0][0]), "dk": np32(runs[0][1]), "dv": np32(runs[0][2])},
+                 {"dq": rdq, "dk": rdk, "dv": rdv}, TOL, "deterministic")

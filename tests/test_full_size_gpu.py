@@ -172,3 +172,23 @@ def test_c5_eight_thread_emulated_ranks_full_size(c5):
     cat = {n: np.concatenate([o[i] for o in outs], axis=1)[:, :, C5_HEADS]
            for i, n in enumerate(("o", "dq", "dk", "dv"))}
     assert_close(cat, {n: ref[n] for n in ("o", "dq", "dk", "dv")}, TOL, "c5 w8 threads")
+
+
+def test_c2_deterministic_backward_full_size():
+    """C2 with deterministic=1: three repeats bit-identical; the gradients
+    equal the default path's up to the fp32 summation order of dQ (whose
+    arrival order the default path does not fix)."""
+    from foundry_trainer_b200 import configs, ops
+    cfg = configs.CONFIGS["c2"]
+    q, k, v, d_o = (t.cuda() for t in configs.make_inputs(cfg))
+    rope = ops.Rope(configs.positions(cfg.txt, cfg.grid).cuda())
+    o, lse = ops.attn_fwd(q, k, v, rope=rope)
+    runs = [ops.attn_bwd(q, k, v, o, d_o, lse, rope=rope, deterministic=True) for _ in range(3)]
+    ref = ops.attn_bwd(q, k, v, o, d_o, lse, rope=rope)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    for rep in runs[1:]:
+        assert all(torch.equal(a, b) for a, b in zip(runs[0], rep))
+    for name, a, b in zip(("dq", "dk", "dv"), runs[0], ref):
+        err = orc.max_rel(np32(a), np32(b))
+        assert err <= 1e-2, (name, err)
