@@ -867,7 +867,9 @@ def main():
                     f"{n_loc} rows per rank, non-causal, axial RoPE")
         parallelism = f"sequence ring x{world} (NCCL send/recv of K,V and fp32 dK,dV)"
     else:
-        launches_per_step = 5  # rope q,k (+ table) + fwd; delta (+ dQ clear) + bwd + dQ finish
+        # (cos, sin) table + fwd (q, k rotated in its tile loads); delta (+ dQ
+        # clear) + bwd + dQ finish
+        launches_per_step = 5
         if batch_mode:
             workload = (f"{cfg.name}: B={cfg.B} H={cfg.H} S={cfg.S} "
                         f"({cfg.txt} text + {cfg.grid}x{cfg.grid} image) D={cfg.D}, the batch "

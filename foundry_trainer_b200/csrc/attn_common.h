@@ -51,11 +51,24 @@ int ensure_smem_attr(const void* fn, int bytes, int kernel_id);
 // bf16 sm_100a kernels
 // merge: 0 plain; 1 (o_acc, lse_acc) <- block; 2 fold block into them;
 // 3 fold, then write o (bf16) and lse (see the kernel's Params)
+// In-tile rotation of q and k (axial RoPE, four 32-wide axes): the kernel
+// rotates each Q and K tile in shared memory as it lands and writes the
+// rotated q and k to q_rot / k_rot ((B, S, H, D) bf16) for the backward.
+// Each K tile is rotated once: the CTA that owns it publishes it to k_rot
+// and sets its flag; other CTAs load the published copy when its flag is
+// set and otherwise rotate the raw tile themselves (nobody waits).
+struct FwdRope {
+  const uint32_t* cs;  // packed bf16 (cos, sin), (S, 64) words
+  const fa_tensor_t* q_rot;
+  const fa_tensor_t* k_rot;
+  uint32_t* k_pub;     // (B, H, ceil(S/128)) flags, zero before the launch
+};
+
 int launch_attn_fwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
                          const fa_tensor_t* k, const fa_tensor_t* v,
                          const fa_tensor_t* o, float* lse, float scale,
                          cudaStream_t stream, int merge = 0, float* o_acc = nullptr,
-                         float* lse_acc = nullptr);
+                         float* lse_acc = nullptr, const FwdRope* rope = nullptr);
 
 // dK/dV rows stored per key segment: row j to dk[j / seg], dv[j / seg] at
 // local row j % seg (fp32 contiguous (B, seg, H, D) each; peers' memory allowed)
@@ -98,6 +111,11 @@ int launch_bwd_delta(int dtype, const AttnShape& sh, const fa_tensor_t* o,
 // (cos, sin) table for tokens [0, S) (+pos_offset), S * n_axes*axis_dim/2 float2
 int launch_rope_table(int dtype, int S, const fa_rope_t* rope, int pos_offset,
                       float2* table, cudaStream_t stream);
+// bf16 path: the float2 table and the packed bf16 (cos, sin) words (cos in
+// bits 0-15, sin in bits 16-31), S * n_axes*axis_dim/2 entries each
+// (it also zeroes `n_clear` words at `clear`: the forward's publish flags)
+int launch_rope_table2(int S, const fa_rope_t* rope, float2* table, uint32_t* packed,
+                       uint32_t* clear, int64_t n_clear, cudaStream_t stream);
 // table may be nullptr (cos/sin evaluated per element)
 int launch_rope(int dtype, const AttnShape& sh, const fa_tensor_t* x,
                 const fa_tensor_t* y, const fa_rope_t* rope, int inverse,

@@ -22,7 +22,22 @@
 //   warp 8      TMA producer of Q0, Q1, K and V (one lane)
 //   warp 9      tcgen05 MMA issuer (the whole warp runs the loop, one
 //               elected lane issues), TMEM owner
-//   warp 10     idle
+//   warps 10-11 RoPE inside the op: rotate a K tile that arrived unrotated
+//               (idle otherwise)
+// With RoPE inside the op (the reference's apply_rope on q and k,
+// crates/foundry-spike/src/lib.rs:122-129, fused into the tile loads), every
+// Q and K tile is rotated once, in shared memory, by the CTA that loads it
+// first: at CTA start softmax warpgroup t rotates Q tile t and this CTA's
+// own K tile t (the first two K tiles it visits; over all CTAs of a head,
+// every K tile), stores them to q_rot / k_rot with TMA (the backward reads
+// them) and publishes the K tiles with a state per (b, h, K tile): 0 the
+// owning CTA has not started, 1 it is running, 2 the rotated tile is in
+// k_rot. The producer loads every other K tile from k_rot when its state is
+// 2, waits for a running owner to publish (bounded, ~20 us) when it is 1,
+// and otherwise loads it unrotated for warps 10-11 to rotate in its slot;
+// no CTA waits on a CTA that has not started, nor unboundedly on any.
+// The (cos, sin) pairs come from a packed bf16 table (one 32-bit word per
+// token and frequency).
 // TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512).
 // P_t (bf16, two per column) is written over the first 64 columns of S_t
 // once the row of S_t is in registers; it is the TMEM A operand of
@@ -41,13 +56,13 @@ constexpr int kKeys = 128;          // keys per K/V tile
 constexpr int kTileBytes = 32768;   // 128 x 128 bf16
 constexpr int kBlkBytes = 16384;    // one 64-column swizzle block
 constexpr int kSlots = 5;           // K/V ring: load n (K_j: n = 2j, V_j: 2j+1) in slot n % 5
-constexpr int kThreads = 352;
+constexpr int kThreads = 384;
 
 // shared memory map (offsets from a 1024-byte aligned base)
 constexpr int kOffQ = 0;  // Q0, Q1; each becomes its tile's O staging at the end
 constexpr int kOffKV = kOffQ + kTiles * kTileBytes;
 constexpr int kOffBar = kOffKV + kSlots * kTileBytes;
-constexpr int kNumBars = 24;
+constexpr int kNumBars = 26;
 constexpr int kOffMisc = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffMisc + 64 + 1024;  // + alignment slack
 
@@ -59,6 +74,11 @@ constexpr int B_SFULL = 11;   // + tile: S_t(j) complete
 constexpr int B_PREADY = 13;  // + tile: softmax wrote P_t(j) (and rescaled O_t)
 constexpr int B_PVDONE = 15;  // + tile: O_t += P_t(j) V_j completed
 constexpr int B_FINAL = 17;
+constexpr int B_KREADY = 18;  // + slot: the K tile (step >= 2) in the slot is rotated
+constexpr int B_QREADY = 23;  // Q tiles and this CTA's own two K tiles rotated (256 arrivals)
+constexpr int B_STORED = 24;  // the stores of this CTA's own K tiles have read their slots (2)
+// polling budget for another CTA's published K tile before rotating it here
+constexpr long long kPubWaitCycles = 40000;
 
 constexpr uint32_t kColS = 0;    // + 128 t
 constexpr uint32_t kColO = 256;  // + 128 t
@@ -70,6 +90,70 @@ constexpr uint32_t kColO = 256;  // + 128 t
 constexpr int kPolyEvery = 0;
 __device__ __forceinline__ constexpr bool poly_column(int c) {
   return kPolyEvery > 0 && c % (kPolyEvery > 0 ? kPolyEvery : 1) == kPolyEvery - 1;
+}
+
+// Rotates, in place, the rows of a (128 rows x 128 head dims) bf16 tile in
+// shared memory laid out as the TMA writes it (two 16 KB SWIZZLE_128B blocks
+// of 64 dims): row r is token token0 + r; rows at or past `limit` are the
+// tile's zero fill and are left alone. Work item (row, axis a, chunk pair u)
+// rotates dims 32a+8u..+7 against 32a+16+8u..+7 with frequencies
+// 16a+8u..+7: y1 = x1 c - x2 s, y2 = x2 c + x1 s, each product and the sum
+// rounded in fp32 (the reference's separate broadcast_mul and add), then
+// rounded to bf16. `cs` holds the packed bf16 (cos, sin) per (token, freq).
+// A thread takes its items NB at a time and issues all of their (cos, sin)
+// loads (L2) and tile loads before computing, so one memory latency is
+// exposed per batch rather than per item.
+template <int NB>
+__device__ __forceinline__ void rope_rotate_tile(uint8_t* tile, const uint32_t* cs, int token0,
+                                                 int limit, int tid, int nthreads) {
+  for (int base = tid; base < 1024; base += NB * nthreads) {
+    uint4 w[NB][2], x[NB][2];
+    bool live[NB];
+#pragma unroll
+    for (int k = 0; k < NB; ++k) {
+      const int task = base + k * nthreads;
+      const int r = task & 127, au = task >> 7, a = au >> 1, u = au & 1;
+      live[k] = task < 1024 && token0 + r < limit;
+      if (live[k]) {
+        const uint4* t4 =
+            reinterpret_cast<const uint4*>(cs + (int64_t)(token0 + r) * 64 + 16 * a + 8 * u);
+        w[k][0] = __ldg(t4);
+        w[k][1] = __ldg(t4 + 1);
+        const uint8_t* blk = tile + (a >> 1) * kBlkBytes;
+        const int c1 = 4 * (a & 1) + u;
+        x[k][0] = *reinterpret_cast<const uint4*>(blk + sw128_offset(r, c1));
+        x[k][1] = *reinterpret_cast<const uint4*>(blk + sw128_offset(r, c1 + 2));
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < NB; ++k) {
+      if (!live[k]) continue;
+      const int task = base + k * nthreads;
+      const int r = task & 127, au = task >> 7, a = au >> 1, u = au & 1;
+      const uint32_t xa[4] = {x[k][0].x, x[k][0].y, x[k][0].z, x[k][0].w};
+      const uint32_t xb[4] = {x[k][1].x, x[k][1].y, x[k][1].z, x[k][1].w};
+      const uint32_t ww[8] = {w[k][0].x, w[k][0].y, w[k][0].z, w[k][0].w,
+                              w[k][1].x, w[k][1].y, w[k][1].z, w[k][1].w};
+      uint32_t ya[4], yb[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint64_t a2 = f2_pack(bf16_lo(xa[q]), bf16_hi(xa[q]));
+        const uint64_t b2 = f2_pack(bf16_lo(xb[q]), bf16_hi(xb[q]));
+        const uint64_t c2 = f2_pack(bf16_lo(ww[2 * q]), bf16_lo(ww[2 * q + 1]));
+        const uint64_t s2 = f2_pack(bf16_hi(ww[2 * q]), bf16_hi(ww[2 * q + 1]));
+        float y0, y1, z0, z1;
+        f2_unpack(fsub2(fmul2(a2, c2), fmul2(b2, s2)), y0, y1);
+        f2_unpack(fadd2(fmul2(b2, c2), fmul2(a2, s2)), z0, z1);
+        ya[q] = pack_bf16(y0, y1);
+        yb[q] = pack_bf16(z0, z1);
+      }
+      uint8_t* blk = tile + (a >> 1) * kBlkBytes;
+      const int c1 = 4 * (a & 1) + u;
+      *reinterpret_cast<uint4*>(blk + sw128_offset(r, c1)) = make_uint4(ya[0], ya[1], ya[2], ya[3]);
+      *reinterpret_cast<uint4*>(blk + sw128_offset(r, c1 + 2)) =
+          make_uint4(yb[0], yb[1], yb[2], yb[3]);
+    }
+  }
 }
 
 // K/V tile visited at step j by the CTA with tile pair `pair`.
@@ -88,13 +172,20 @@ struct Params {
   int merge;
   float* o_acc;      // fp32 contiguous (B, S, H, D), normalised rows
   float* lse_acc;    // (B, H, S), natural log
+  // RoPE inside (plain mode, kv_len == S): packed bf16 (cos, sin) per
+  // (token, frequency), 64 words per token; nullptr: q, k used as given
+  const uint32_t* rope_cs;
+  // per (b, h, K tile): set once the tile's rotated copy is in k_rot
+  uint32_t* k_pub;
 };
 
 __global__ void __launch_bounds__(kThreads, 1)
 attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                 const __grid_constant__ CUtensorMap tm_k,
                 const __grid_constant__ CUtensorMap tm_v,
-                const __grid_constant__ CUtensorMap tm_o, Params p) {
+                const __grid_constant__ CUtensorMap tm_o,
+                const __grid_constant__ CUtensorMap tm_qr,
+                const __grid_constant__ CUtensorMap tm_kr, Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -102,6 +193,9 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc);
   volatile int* abort_flag =
       reinterpret_cast<volatile int*>(smem + kOffMisc + 4);
+  // per ring slot, with RoPE inside: 1 = the K tile in the slot is raw and
+  // is rotated here, 0 = it is another CTA's published rotated copy
+  volatile int* rot_mark = reinterpret_cast<volatile int*>(smem + kOffMisc + 16);
 
   const int warp = warp_id();
   const int lane = lane_id();
@@ -122,6 +216,9 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
       mbar_init(&bars[B_PVDONE + t], 1);
     }
     mbar_init(&bars[B_FINAL], 1);
+    for (int s = 0; s < kSlots; ++s) mbar_init(&bars[B_KREADY + s], 64);
+    mbar_init(&bars[B_QREADY], 256);
+    mbar_init(&bars[B_STORED], 2);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -140,6 +237,13 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
+      if (p.rope_cs != nullptr) {
+        // this CTA's own K tiles (steps 0 and 1) are being rotated here: a
+        // CTA that needs them waits for their publication instead of rotating
+        uint32_t* pub = p.k_pub + ((int64_t)b * p.H + h) * nkv;
+        atom_max_relaxed_gpu(pub + kv_tile_of(0, pair, nkv), 1u);
+        if (nkv > 1) atom_max_relaxed_gpu(pub + kv_tile_of(1, pair, nkv), 1u);
+      }
       const int row = pair * kTiles * kRows;
       mbar_arrive_expect_tx(&bars[B_Q], kTiles * kTileBytes);
       for (int t = 0; t < kTiles; ++t) {
@@ -152,10 +256,33 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
         if (*abort_flag) break;
         const int s = n % kSlots, u = n / kSlots;
         if (n >= kSlots && !(ok = mbar_wait(&bars[B_EMPTY + s], (u - 1) & 1))) break;
+        // the slots of the first two K tiles are stored to k_rot from shared
+        // memory: their first reuse waits until those stores have read them
+        if (p.rope_cs != nullptr && n == kSlots && !(ok = mbar_wait(&bars[B_STORED], 0))) break;
         uint8_t* d = smem + kOffKV + s * kTileBytes;
+        const int kvt = kv_tile_of(n >> 1, pair, nkv);
         const CUtensorMap* tm = (n & 1) ? &tm_v : &tm_k;
+        if (!(n & 1) && p.rope_cs != nullptr) {
+          // a K tile other than this CTA's own two: its rotated copy when
+          // the CTA that owns it has published it (checked, never waited for)
+          bool published = false;
+          if ((n >> 1) >= 2) {
+            const uint32_t* flag = p.k_pub + ((int64_t)b * p.H + h) * nkv + kvt;
+            uint32_t state = ld_acquire_gpu(flag);
+            if (state == 1u) {  // the owner runs: it publishes within a step or two
+              const long long t0 = clock64();
+              while ((state = ld_acquire_gpu(flag)) == 1u && clock64() - t0 < kPubWaitCycles &&
+                     !*abort_flag)
+                __nanosleep(128);
+            }
+            published = state == 2u;
+            if (published) fence_proxy_async_global();
+          }
+          rot_mark[s] = published ? 0 : 1;
+          if (published) tm = &tm_kr;
+        }
         mbar_arrive_expect_tx(&bars[B_FULL + s], kTileBytes);
-        const int kvrow = kv_tile_of(n >> 1, pair, nkv) * kKeys;
+        const int kvrow = kvt * kKeys;
         tma_load_4d(d, tm, &bars[B_FULL + s], 0, kvrow, h, b);
         tma_load_4d(d + kBlkBytes, tm, &bars[B_FULL + s], 64, kvrow, h, b);
       }
@@ -166,14 +293,26 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
     {
       constexpr uint32_t kIdescS = idesc_bf16(128, 128, false, false);
       constexpr uint32_t kIdescO = idesc_bf16(128, 128, false, true);
-      bool ok = mbar_wait_w(&bars[B_Q], 0);
+      const bool rotate = p.rope_cs != nullptr;
+      bool ok = mbar_wait_w(&bars[B_Q], 0);  // (with RoPE: QREADY, waited in issue_s)
       tc_fence_after();
       // S_t(j) = Q_t K_j^T. It overwrites P_t(j-1), which PV_t(j-1) reads:
       // tcgen05.mma operations issued by one thread execute in issue order,
       // so S_t(j) is issued right behind PV_t(j-1) without waiting for it.
+      // With RoPE inside, K_j is used once rotated (KREADY of its slot: the
+      // slot holds K tiles at steps j, j+5, ..., so that barrier's phase is
+      // j / 5) and Q_t once its warpgroup has rotated it (QREADY).
       auto issue_s = [&](int t, int j) -> bool {
         const int s = (2 * j) % kSlots, u = (2 * j) / kSlots;
-        if (t == 0 && !mbar_wait_w(&bars[B_FULL + s], u & 1)) return false;
+        if (t == 0) {
+          // RoPE inside: steps 0, 1 use the tiles the softmax warpgroups
+          // rotated (QREADY); a slot holds a later K tile at steps j, j+5,
+          // ..., so its KREADY phase is (j - 2) / 5
+          if (rotate ? (j < 2 ? (j == 0 && !mbar_wait_w(&bars[B_QREADY], 0))
+                              : !mbar_wait_w(&bars[B_KREADY + s], ((j - 2) / kSlots) & 1))
+                     : !mbar_wait_w(&bars[B_FULL + s], u & 1))
+            return false;
+        }
         tc_fence_after();
         const uint32_t q_base = smem_u32(smem + kOffQ + t * kTileBytes);
         const uint32_t k_base = smem_u32(smem + kOffKV + s * kTileBytes);
@@ -230,7 +369,49 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
     float m_run = -INFINITY;
     float l_run = 0.f;
     bool failed = false;
+    const bool own_k = p.rope_cs != nullptr && t < nkv;  // this warpgroup rotates own K tile t
+    if (p.rope_cs != nullptr) {
+      // RoPE inside: rotate Q tile t and this CTA's own K tile t (the K tile
+      // of step t, in ring slot 2t) in place, store both to q_rot / k_rot
+      uint8_t* qt = smem + kOffQ + t * kTileBytes;
+      uint8_t* kt = smem + kOffKV + 2 * t * kTileBytes;
+      const int q_row0 = (pair * kTiles + t) * kRows;
+      const int k_row0 = kv_tile_of(t, pair, nkv) * kKeys;
+      bool stop = !mbar_wait(&bars[B_Q], 0);
+      if (!stop && own_k) stop = !mbar_wait(&bars[B_FULL + 2 * t], 0);
+      stop = __any_sync(0xffffffffu, stop);
+      if (!stop) {
+        rope_rotate_tile<8>(qt, p.rope_cs, q_row0, p.S, row_in_tile, 128);
+        if (own_k) rope_rotate_tile<8>(kt, p.rope_cs, k_row0, p.kv_len, row_in_tile, 128);
+      }
+      fence_proxy_async_smem();
+      if (named_bar_any(bar_id, 128, stop)) {
+        failed = true;
+      } else if (warp == 4 * t && lane == 0) {
+        tma_store_4d(&tm_qr, qt, 0, q_row0, h, b);
+        tma_store_4d(&tm_qr, qt + kBlkBytes, 64, q_row0, h, b);
+        if (own_k) {
+          tma_store_4d(&tm_kr, kt, 0, k_row0, h, b);
+          tma_store_4d(&tm_kr, kt + kBlkBytes, 64, k_row0, h, b);
+        }
+        bulk_commit_group();
+      }
+      mbar_arrive(&bars[B_QREADY]);
+      if (warp == 4 * t && lane == 0) {
+        // the producer reuses the K slots only once these stores have read them
+        bulk_wait_group_read0();
+        mbar_arrive(&bars[B_STORED]);
+      }
+    }
     for (int j = 0; j < nkv; ++j) {
+      if (j == 1 && own_k && warp == 4 * t && lane == 0 && !failed) {
+        // a step later the K store has completed (no wait in practice):
+        // publish the tile (a proxy fence orders the TMA writes before the
+        // release of the flag)
+        bulk_wait_group0();
+        fence_proxy_async_global();
+        st_release_gpu(p.k_pub + ((int64_t)b * p.H + h) * nkv + kv_tile_of(t, pair, nkv), 2u);
+      }
       bool stop = failed || *abort_flag != 0;
       if (!stop) stop = !mbar_wait(&bars[B_SFULL + t], j & 1);
       if (__any_sync(0xffffffffu, stop)) { failed = true; break; }
@@ -315,6 +496,9 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
     bool stop = failed || *abort_flag != 0;
     if (!stop) stop = !mbar_wait(&bars[B_PVDONE + t], (nkv - 1) & 1);
     stop = __any_sync(0xffffffffu, stop);
+    // (the rotation flag is re-read from the parameters: no register held
+    // across the loop)
+    if (p.rope_cs != nullptr && warp == 4 * t && lane == 0) bulk_wait_group_read0();
     if (!named_bar_any(bar_id, 128, stop)) {
       tc_fence_after();
       const int row0 = (pair * kTiles + t) * kRows;
@@ -391,6 +575,26 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
     } else {
       *abort_flag = 1;
     }
+    if (p.rope_cs != nullptr && warp == 4 * t && lane == 0) bulk_wait_group0();
+  } else if (warp >= 10) {
+    // ---------- RoPE inside: rotate the K tiles of steps >= 2 that arrived
+    // unrotated (their owner had not published them in time)
+    if (p.rope_cs != nullptr) {
+      const int tid = threadIdx.x - 320;  // 0..63
+      bool ok = true;
+      for (int j = 2; j < nkv; ++j) {
+        const int n = 2 * j, s = n % kSlots, u = n / kSlots;
+        if (__any_sync(0xffffffffu, *abort_flag != 0)) { ok = false; break; }
+        if (!(ok = mbar_wait_w(&bars[B_FULL + s], u & 1))) break;
+        if (rot_mark[s]) {
+          rope_rotate_tile<8>(smem + kOffKV + s * kTileBytes, p.rope_cs,
+                              kv_tile_of(j, pair, nkv) * kKeys, p.kv_len, tid, 64);
+          fence_proxy_async_smem();
+        }
+        mbar_arrive(&bars[B_KREADY + s]);
+      }
+      if (!ok) *abort_flag = 1;
+    }
   }
 
   tc_fence_before();
@@ -408,13 +612,19 @@ int launch_attn_fwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
                          const fa_tensor_t* k, const fa_tensor_t* v,
                          const fa_tensor_t* o, float* lse, float scale,
                          cudaStream_t stream, int merge, float* o_acc,
-                         float* lse_acc) {
-  CUtensorMap tq, tk, tv, to;
+                         float* lse_acc, const FwdRope* rope) {
+  if (rope != nullptr &&
+      (merge != 0 || kv_len != sh.S || rope->cs == nullptr || rope->k_pub == nullptr))
+    return FA_ERR_INVALID_ARG;  // in-tile rotation: plain mode, q and k share positions
+  CUtensorMap tq, tk, tv, to, tqr, tkr;
   int rc = make_tmap_bshd(&tq, q, sh.B, sh.S, sh.H, sh.D, 128);
   if (!rc) rc = make_tmap_bshd(&tk, k, sh.B, kv_len, sh.H, sh.D, 128);
   if (!rc) rc = make_tmap_bshd(&tv, v, sh.B, kv_len, sh.H, sh.D, 128);
   // modes 1 and 2 write no bf16 O: the map is encoded over q and never used
   if (!rc) rc = make_tmap_bshd(&to, (merge == 1 || merge == 2) ? q : o, sh.B, sh.S, sh.H, sh.D, 128);
+  // the rotated-q/k maps exist only with RoPE inside (else never used)
+  if (!rc) rc = make_tmap_bshd(&tqr, rope ? rope->q_rot : q, sh.B, sh.S, sh.H, sh.D, 128);
+  if (!rc) rc = make_tmap_bshd(&tkr, rope ? rope->k_rot : q, sh.B, sh.S, sh.H, sh.D, 128);
   if (rc) return rc;
   fwd::Params p;
   p.S = sh.S;
@@ -426,13 +636,15 @@ int launch_attn_fwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
   p.merge = merge;
   p.o_acc = o_acc;
   p.lse_acc = lse_acc;
+  p.rope_cs = rope ? rope->cs : nullptr;
+  p.k_pub = rope ? rope->k_pub : nullptr;
   rc = ensure_smem_attr((const void*)fwd::attn_fwd_kernel, fwd::kSmemBytes,
                         kKernelFwdBf16);
   if (rc) return rc;
   constexpr int kRowsPerCta = fwd::kTiles * fwd::kRows;
   dim3 grid((sh.S + kRowsPerCta - 1) / kRowsPerCta, sh.H, sh.B);
   fwd::attn_fwd_kernel<<<grid, fwd::kThreads, fwd::kSmemBytes, stream>>>(
-      tq, tk, tv, to, p);
+      tq, tk, tv, to, tqr, tkr, p);
   return launch_status();
 }
 

@@ -261,12 +261,23 @@ int fa_device_status(void) {
   return first;
 }
 
-// forward workspace (RoPE inside the op): [q_rot | k_rot | (cos, sin) table]
+// bf16 forward with the reference's rope layout (four 32-wide axes): the
+// rotation runs inside the forward kernel's tile loads
+static bool fused_fwd_rope(int dtype, const fa_rope_t* rope, int D) {
+  return dtype == FA_DTYPE_BF16 && rope != nullptr && D == 128 && rope->n_axes == 4 &&
+         rope->axis_dim == 32;
+}
+
+// forward workspace (RoPE inside the op): [q_rot | k_rot | (cos, sin) table
+// (float2) | the same as packed bf16 pairs (in-kernel rotation only)]
 size_t fa_fwd_workspace_bytes(int dtype, int B, int S, int H, int D,
                               const fa_rope_t* rope) {
   if (rope == nullptr) return 0;
   const size_t es = dtype == FA_DTYPE_BF16 ? 2 : 4;
-  return 2 * align256((size_t)B * S * H * D * es) + rope_table_bytes(S, rope);
+  size_t total = 2 * align256((size_t)B * S * H * D * es) + rope_table_bytes(S, rope);
+  if (fused_fwd_rope(dtype, rope, D))  // + packed table + per-K-tile publish flags
+    total += rope_table_bytes(S, rope) / 2 + align256((size_t)B * H * ((S + 127) / 128) * 4);
+  return total;
 }
 
 int fa_fwd(int dtype, int B, int S, int H, int D, const fa_tensor_t* q,
@@ -294,8 +305,22 @@ int fa_fwd(int dtype, int B, int S, int H, int D, const fa_tensor_t* q,
     const size_t tb = align256((size_t)B * S * H * D * es);
     qr = contiguous_view(ws, S, H, D);
     kr = contiguous_view(ws + tb, S, H, D);
-    // the rotation pass also leaves the (cos, sin) table for fa_bwd_saved
     float2* table = reinterpret_cast<float2*>(ws + 2 * tb);
+    if (fused_fwd_rope(dtype, rope, D)) {
+      // the kernel rotates q and k in its tile loads and writes q_rot and
+      // k_rot; the table pass also leaves the float2 table for fa_bwd_saved
+      uint32_t* packed = reinterpret_cast<uint32_t*>(ws + 2 * tb + rope_table_bytes(S, rope));
+      uint32_t* k_pub = packed + rope_table_bytes(S, rope) / 8;
+      const int64_t n_pub = (int64_t)B * H * ((S + 127) / 128);
+      FA_TRY(launch_rope_table2(S, rope, table, packed, k_pub, n_pub, st));
+      const FwdRope fr{packed, &qr, &kr, k_pub};
+      cudaEvent_t stop = timer_begin(FA_TIMER_FWD, st);
+      const int rc = launch_attn_fwd_bf16(sh, S, q, k, v, o, lse, scale, st, 0, nullptr,
+                                          nullptr, &fr);
+      timer_end(stop, st);
+      return rc;
+    }
+    // the rotation pass also leaves the (cos, sin) table for fa_bwd_saved
     FA_TRY(launch_rope_pair(dtype, sh, q, &qr, k, &kr, rope, 0, 0, st, nullptr, table));
   }
   cudaEvent_t stop = timer_begin(FA_TIMER_FWD, st);

@@ -8,6 +8,8 @@
 // head-dim columns {l, l+32, l+64, l+96} so loads are coalesced and the
 // rotate-half partner of column d (d +- 16 inside a 32-wide axis segment) is
 // lane l ^ 16 holding the same slot.
+#include <algorithm>
+
 #include "attn_common.h"
 #include "rope.cuh"
 #include "sm100_ptx.cuh"
@@ -116,6 +118,23 @@ __global__ void rope_table_kernel(const __grid_constant__ RopeArgs r, int S, flo
   if (i >= (int64_t)S * nf) return;
   const int t = (int)(i / nf), f = (int)(i % nf);
   table[(int64_t)(t + r.pos_offset) * nf + f] = rope_cs_direct(r, t, f);
+}
+
+// The same table, and beside it the bf16 (cos, sin) pairs of the bf16 path
+// packed in one 32-bit word per (token, frequency): cos in the low half, sin
+// in the high half (exact: the values are already rounded to bf16). The
+// forward kernel's in-tile rotation reads the packed form.
+__global__ void rope_table2_kernel(const __grid_constant__ RopeArgs r, int S, float2* table,
+                                   uint32_t* packed, uint32_t* clear, int64_t n_clear) {
+  const int nf = r.n_axes * (r.axis_dim >> 1);
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n_clear) clear[i] = 0u;
+  if (i >= (int64_t)S * nf) return;
+  const int t = (int)(i / nf), f = (int)(i % nf);
+  const float2 cs = rope_cs_direct(r, t, f);
+  const int64_t o = (int64_t)(t + r.pos_offset) * nf + f;
+  table[o] = cs;
+  packed[o] = (__float_as_uint(cs.x) >> 16) | (__float_as_uint(cs.y) & 0xFFFF0000u);
 }
 
 // ------------------------------------------------ token-major fast paths
@@ -684,6 +703,15 @@ int launch_rope_table(int dtype, int S, const fa_rope_t* rope, int pos_offset,
   const RopeArgs r = make_rope_args(rope, dtype == FA_DTYPE_BF16 ? 1 : 0, pos_offset);
   const int64_t n = (int64_t)S * r.n_axes * (r.axis_dim / 2);
   misc::rope_table_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(r, S, table);
+  return launch_status();
+}
+
+int launch_rope_table2(int S, const fa_rope_t* rope, float2* table, uint32_t* packed,
+                       uint32_t* clear, int64_t n_clear, cudaStream_t stream) {
+  const RopeArgs r = make_rope_args(rope, 1, 0);
+  const int64_t n = std::max<int64_t>((int64_t)S * r.n_axes * (r.axis_dim / 2), n_clear);
+  misc::rope_table2_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(r, S, table, packed,
+                                                                           clear, n_clear);
   return launch_status();
 }
 

@@ -206,3 +206,36 @@ def test_bf16_deterministic_backward_repeats_bit_identical(B, S, H, with_rope):
                                                 rope_pos=pos.numpy() if pos is not None else None)
     assert_close({"dq": np32(runs[0][0]), "dk": np32(runs[0][1]), "dv": np32(runs[0][2])},
                  {"dq": rdq, "dk": rdk, "dv": rdv}, TOL, "deterministic")
+
+
+@pytest.mark.parametrize("B,S,H", [(1, 1, 1), (1, 128, 2), (2, 130, 3), (1, 333, 2), (1, 1000, 2)])
+def test_bf16_forward_in_tile_rotation_matches_rope_apply(B, S, H):
+    """With RoPE inside, the forward rotates q and k in its tile loads and
+    leaves them in its workspace for the backward. They are bit-identical to
+    the standalone rotation (fa_rope_apply: the reference's apply_rope,
+    lib.rs:122-129) at sizes with one, two, three (odd: a tile stored by two
+    CTAs) and eight K tiles and ragged last tiles; O, LSE against the oracle."""
+    from foundry_trainer_b200 import ops
+    g = torch.Generator().manual_seed(41 + S)
+    shape = (B, S, H, 128)
+    q, k, v = ((torch.randn(shape, generator=g) * 0.5).to(torch.bfloat16).cuda() for _ in range(3))
+    pos = torch.zeros((S, 4))
+    pos[:, 1] = torch.arange(S).float() // 20
+    pos[:, 2] = torch.arange(S).float() % 20
+    pos[:, 0] = (torch.arange(S) % 3).float()
+    rope = ops.Rope(pos.cuda())
+    saved = {}
+    o, lse = ops.attn_fwd(q, k, v, rope=rope, saved=saved)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    ws = saved["ws"]
+    n = B * S * H * 128
+    tb = (n * 2 + 255) // 256 * 256
+    q_rot = ws[:n * 2].view(torch.bfloat16).view(shape)
+    k_rot = ws[tb:tb + n * 2].view(torch.bfloat16).view(shape)
+    assert torch.equal(q_rot, ops.rope_apply(q, rope))
+    assert torch.equal(k_rot, ops.rope_apply(k, rope))
+    d_o = torch.zeros_like(q)
+    ro, rlse, _, _, _ = orc.attn_fwd_bwd_bshd(np32(q), np32(k), np32(v), np32(d_o), "f32",
+                                              rope_pos=pos.numpy())
+    assert_close({"o": np32(o), "lse": np32(lse)}, {"o": ro, "lse": rlse}, TOL, "fused rope fwd")
