@@ -62,13 +62,18 @@ constexpr int kThreads = 384;
 constexpr int kOffQ = 0;  // Q0, Q1; each becomes its tile's O staging at the end
 constexpr int kOffKV = kOffQ + kTiles * kTileBytes;
 constexpr int kOffBar = kOffKV + kSlots * kTileBytes;
-constexpr int kNumBars = 26;
+constexpr int kNumBars = 32;
 constexpr int kOffMisc = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffMisc + 64 + 1024;  // + alignment slack
 
 // barrier indices
+// A ring slot alternates K and V loads (load n goes to slot n % 5), so the
+// arrivals of K tiles and of V tiles are signalled on separate barriers: a
+// waiter then sees every phase of a barrier it waits on, in order (a parity
+// wait that skipped phases could return for the wrong one), and the phase
+// of load n is n / 10 for both kinds.
 constexpr int B_Q = 0;
-constexpr int B_FULL = 1;     // + slot (5)
+constexpr int B_FULL = 1;     // + slot (5): a V tile landed in the slot
 constexpr int B_EMPTY = 6;    // + slot (5)
 constexpr int B_SFULL = 11;   // + tile: S_t(j) complete
 constexpr int B_PREADY = 13;  // + tile: softmax wrote P_t(j) (and rescaled O_t)
@@ -77,6 +82,7 @@ constexpr int B_FINAL = 17;
 constexpr int B_KREADY = 18;  // + slot: the K tile (step >= 2) in the slot is rotated
 constexpr int B_QREADY = 23;  // Q tiles and this CTA's own two K tiles rotated (256 arrivals)
 constexpr int B_STORED = 24;  // the stores of this CTA's own K tiles have read their slots (2)
+constexpr int B_KFULL = 25;   // + slot (5): a K tile landed in the slot
 // polling budget for another CTA's published K tile before rotating it here
 constexpr long long kPubWaitCycles = 40000;
 
@@ -208,6 +214,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
     mbar_init(&bars[B_Q], 1);
     for (int s = 0; s < kSlots; ++s) {
       mbar_init(&bars[B_FULL + s], 1);
+      mbar_init(&bars[B_KFULL + s], 1);
       mbar_init(&bars[B_EMPTY + s], 1);
     }
     for (int t = 0; t < kTiles; ++t) {
@@ -281,10 +288,11 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
           rot_mark[s] = published ? 0 : 1;
           if (published) tm = &tm_kr;
         }
-        mbar_arrive_expect_tx(&bars[B_FULL + s], kTileBytes);
+        uint64_t* full = &bars[((n & 1) ? B_FULL : B_KFULL) + s];
+        mbar_arrive_expect_tx(full, kTileBytes);
         const int kvrow = kvt * kKeys;
-        tma_load_4d(d, tm, &bars[B_FULL + s], 0, kvrow, h, b);
-        tma_load_4d(d + kBlkBytes, tm, &bars[B_FULL + s], 64, kvrow, h, b);
+        tma_load_4d(d, tm, full, 0, kvrow, h, b);
+        tma_load_4d(d + kBlkBytes, tm, full, 64, kvrow, h, b);
       }
       if (!ok) *abort_flag = 1;
     }
@@ -303,14 +311,14 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
       // slot holds K tiles at steps j, j+5, ..., so that barrier's phase is
       // j / 5) and Q_t once its warpgroup has rotated it (QREADY).
       auto issue_s = [&](int t, int j) -> bool {
-        const int s = (2 * j) % kSlots, u = (2 * j) / kSlots;
+        const int s = (2 * j) % kSlots;
         if (t == 0) {
           // RoPE inside: steps 0, 1 use the tiles the softmax warpgroups
           // rotated (QREADY); a slot holds a later K tile at steps j, j+5,
           // ..., so its KREADY phase is (j - 2) / 5
           if (rotate ? (j < 2 ? (j == 0 && !mbar_wait_w(&bars[B_QREADY], 0))
                               : !mbar_wait_w(&bars[B_KREADY + s], ((j - 2) / kSlots) & 1))
-                     : !mbar_wait_w(&bars[B_FULL + s], u & 1))
+                     : !mbar_wait_w(&bars[B_KFULL + s], (2 * j / 10) & 1))
             return false;
         }
         tc_fence_after();
@@ -327,8 +335,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
       };
       // O_t += P_t(j) V_j
       auto issue_pv = [&](int t, int j) -> bool {
-        const int s = (2 * j + 1) % kSlots, u = (2 * j + 1) / kSlots;
-        if (t == 0 && !mbar_wait_w(&bars[B_FULL + s], u & 1)) return false;
+        const int s = (2 * j + 1) % kSlots;
+        if (t == 0 && !mbar_wait_w(&bars[B_FULL + s], ((2 * j + 1) / 10) & 1)) return false;
         if (!mbar_wait_w(&bars[B_PREADY + t], j & 1)) return false;
         tc_fence_after();
         const uint32_t v_base = smem_u32(smem + kOffKV + s * kTileBytes);
@@ -378,7 +386,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
       const int q_row0 = (pair * kTiles + t) * kRows;
       const int k_row0 = kv_tile_of(t, pair, nkv) * kKeys;
       bool stop = !mbar_wait(&bars[B_Q], 0);
-      if (!stop && own_k) stop = !mbar_wait(&bars[B_FULL + 2 * t], 0);
+      if (!stop && own_k) stop = !mbar_wait(&bars[B_KFULL + 2 * t], 0);
       stop = __any_sync(0xffffffffu, stop);
       if (!stop) {
         rope_rotate_tile<8>(qt, p.rope_cs, q_row0, p.S, row_in_tile, 128);
@@ -582,10 +590,14 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
     if (p.rope_cs != nullptr) {
       const int tid = threadIdx.x - 320;  // 0..63
       bool ok = true;
-      for (int j = 2; j < nkv; ++j) {
-        const int n = 2 * j, s = n % kSlots, u = n / kSlots;
+      // every K tile's arrival is waited for in order (also those of steps
+      // 0 and 1, which the softmax warpgroups rotate), so no phase of a K
+      // barrier is ever skipped
+      for (int j = 0; j < nkv; ++j) {
+        const int n = 2 * j, s = n % kSlots;
         if (__any_sync(0xffffffffu, *abort_flag != 0)) { ok = false; break; }
-        if (!(ok = mbar_wait_w(&bars[B_FULL + s], u & 1))) break;
+        if (!(ok = mbar_wait_w(&bars[B_KFULL + s], (n / 10) & 1))) break;
+        if (j < 2) continue;
         if (rot_mark[s]) {
           rope_rotate_tile<8>(smem + kOffKV + s * kTileBytes, p.rope_cs,
                               kv_tile_of(j, pair, nkv) * kKeys, p.kv_len, tid, 64);
