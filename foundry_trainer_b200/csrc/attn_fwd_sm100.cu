@@ -37,7 +37,8 @@
 // and otherwise loads it unrotated for warps 10-11 to rotate in its slot;
 // no CTA waits on a CTA that has not started, nor unboundedly on any.
 // The (cos, sin) pairs come from a packed bf16 table (one 32-bit word per
-// token and frequency).
+// token and frequency); a Q tile and the K tile of the same tokens are
+// rotated in one pass over the table.
 // TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512).
 // P_t (bf16, two per column) is written over the first 64 columns of S_t
 // once the row of S_t is in registers; it is the TMEM A operand of
@@ -98,66 +99,93 @@ __device__ __forceinline__ constexpr bool poly_column(int c) {
   return kPolyEvery > 0 && c % (kPolyEvery > 0 ? kPolyEvery : 1) == kPolyEvery - 1;
 }
 
-// Rotates, in place, the rows of a (128 rows x 128 head dims) bf16 tile in
-// shared memory laid out as the TMA writes it (two 16 KB SWIZZLE_128B blocks
-// of 64 dims): row r is token token0 + r; rows at or past `limit` are the
-// tile's zero fill and are left alone. Work item (row, axis a, chunk pair u)
-// rotates dims 32a+8u..+7 against 32a+16+8u..+7 with frequencies
-// 16a+8u..+7: y1 = x1 c - x2 s, y2 = x2 c + x1 s, each product and the sum
-// rounded in fp32 (the reference's separate broadcast_mul and add), then
-// rounded to bf16. `cs` holds the packed bf16 (cos, sin) per (token, freq).
-// A thread takes its items NB at a time and issues all of their (cos, sin)
-// loads (L2) and tile loads before computing, so one memory latency is
-// exposed per batch rather than per item.
+// Rotates, in place, the rows of one or two (128 rows x 128 head dims) bf16
+// tiles in shared memory laid out as the TMA writes them (two 16 KB
+// SWIZZLE_128B blocks of 64 dims each); row r of both tiles is token
+// token0 + r (`tb`, when given, is the K tile of the same tokens as the Q
+// tile `ta`: the (cos, sin) pairs are read once for both). Rows at or past
+// `limit` are the tiles' zero fill and are left alone. Work item (row r,
+// axis a, chunk pair u) rotates dims 32a+8u..+7 against 32a+16+8u..+7 with
+// frequencies 16a+8u..+7: y1 = x1 c - x2 s, y2 = x2 c + x1 s, each product
+// and the sum rounded in fp32 (the reference's separate broadcast_mul and
+// add), then rounded to bf16.
+// The eight items of a row are eight consecutive lanes (one quarter-warp):
+// their 32 (cos, sin) words are the token's 256-byte table row, read as two
+// 128-byte runs (`cs` is the packed table, in the order rope_table2_kernel
+// writes it: per token, words 4i..4i+3 = frequencies 8i..8i+3 and words
+// 32+4i.. = 8i+4..8i+7), and their 16-byte chunk accesses cover the eight
+// bank groups of a row — the items of the second 64-dim block take their two
+// chunks in the opposite order (x2 first), which the sign of s absorbs:
+// out_A = x_A c + x_B s', out_B = x_B c - x_A s' with s' = -s when x_A = x1
+// and s' = s when x_A = x2 (the same roundings as y1, y2: a - b = a + (-b)
+// and x (-s) = -(x s) exactly). A thread issues the loads of NB items
+// before computing them, so one memory latency is exposed per batch.
 template <int NB>
-__device__ __forceinline__ void rope_rotate_tile(uint8_t* tile, const uint32_t* cs, int token0,
-                                                 int limit, int tid, int nthreads) {
+__device__ __forceinline__ void rope_rotate_rows(uint8_t* ta, uint8_t* tb, const uint32_t* cs,
+                                                 int token0, int limit, int tid, int nthreads) {
   for (int base = tid; base < 1024; base += NB * nthreads) {
-    uint4 w[NB][2], x[NB][2];
+    uint4 w[NB][2], xa[NB][2], xb[NB][2];
     bool live[NB];
 #pragma unroll
     for (int k = 0; k < NB; ++k) {
       const int task = base + k * nthreads;
-      const int r = task & 127, au = task >> 7, a = au >> 1, u = au & 1;
+      const int r = task >> 3, au = task & 7, a = au >> 1, u = au & 1, hi = a >> 1;
       live[k] = task < 1024 && token0 + r < limit;
       if (live[k]) {
-        const uint4* t4 =
-            reinterpret_cast<const uint4*>(cs + (int64_t)(token0 + r) * 64 + 16 * a + 8 * u);
-        w[k][0] = __ldg(t4);
-        w[k][1] = __ldg(t4 + 1);
-        const uint8_t* blk = tile + (a >> 1) * kBlkBytes;
+        const uint32_t* row = cs + (int64_t)(token0 + r) * 64;
+        w[k][0] = __ldg(reinterpret_cast<const uint4*>(row + 4 * au));
+        w[k][1] = __ldg(reinterpret_cast<const uint4*>(row + 32 + 4 * au));
         const int c1 = 4 * (a & 1) + u;
-        x[k][0] = *reinterpret_cast<const uint4*>(blk + sw128_offset(r, c1));
-        x[k][1] = *reinterpret_cast<const uint4*>(blk + sw128_offset(r, c1 + 2));
+        const uint32_t oA = hi * kBlkBytes + sw128_offset(r, hi ? c1 + 2 : c1);
+        const uint32_t oB = hi * kBlkBytes + sw128_offset(r, hi ? c1 : c1 + 2);
+        xa[k][0] = *reinterpret_cast<const uint4*>(ta + oA);
+        xa[k][1] = *reinterpret_cast<const uint4*>(ta + oB);
+        if (tb != nullptr) {
+          xb[k][0] = *reinterpret_cast<const uint4*>(tb + oA);
+          xb[k][1] = *reinterpret_cast<const uint4*>(tb + oB);
+        }
       }
     }
 #pragma unroll
     for (int k = 0; k < NB; ++k) {
       if (!live[k]) continue;
       const int task = base + k * nthreads;
-      const int r = task & 127, au = task >> 7, a = au >> 1, u = au & 1;
-      const uint32_t xa[4] = {x[k][0].x, x[k][0].y, x[k][0].z, x[k][0].w};
-      const uint32_t xb[4] = {x[k][1].x, x[k][1].y, x[k][1].z, x[k][1].w};
-      const uint32_t ww[8] = {w[k][0].x, w[k][0].y, w[k][0].z, w[k][0].w,
-                              w[k][1].x, w[k][1].y, w[k][1].z, w[k][1].w};
-      uint32_t ya[4], yb[4];
+      const int r = task >> 3, au = task & 7, a = au >> 1, u = au & 1, hi = a >> 1;
+      // s' = -s for the first block's items (sin is the high half of a word)
+      const uint32_t flip = hi ? 0u : 0x80000000u;
+      const uint32_t ww[8] = {w[k][0].x ^ flip, w[k][0].y ^ flip, w[k][0].z ^ flip,
+                              w[k][0].w ^ flip, w[k][1].x ^ flip, w[k][1].y ^ flip,
+                              w[k][1].z ^ flip, w[k][1].w ^ flip};
+      uint64_t c2[4], s2[4];
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        const uint64_t a2 = f2_pack(bf16_lo(xa[q]), bf16_hi(xa[q]));
-        const uint64_t b2 = f2_pack(bf16_lo(xb[q]), bf16_hi(xb[q]));
-        const uint64_t c2 = f2_pack(bf16_lo(ww[2 * q]), bf16_lo(ww[2 * q + 1]));
-        const uint64_t s2 = f2_pack(bf16_hi(ww[2 * q]), bf16_hi(ww[2 * q + 1]));
-        float y0, y1, z0, z1;
-        f2_unpack(fsub2(fmul2(a2, c2), fmul2(b2, s2)), y0, y1);
-        f2_unpack(fadd2(fmul2(b2, c2), fmul2(a2, s2)), z0, z1);
-        ya[q] = pack_bf16(y0, y1);
-        yb[q] = pack_bf16(z0, z1);
+        c2[q] = f2_pack(bf16_lo(ww[2 * q]), bf16_lo(ww[2 * q + 1]));
+        s2[q] = f2_pack(bf16_hi(ww[2 * q]), bf16_hi(ww[2 * q + 1]));
       }
-      uint8_t* blk = tile + (a >> 1) * kBlkBytes;
       const int c1 = 4 * (a & 1) + u;
-      *reinterpret_cast<uint4*>(blk + sw128_offset(r, c1)) = make_uint4(ya[0], ya[1], ya[2], ya[3]);
-      *reinterpret_cast<uint4*>(blk + sw128_offset(r, c1 + 2)) =
-          make_uint4(yb[0], yb[1], yb[2], yb[3]);
+      const uint32_t oA = hi * kBlkBytes + sw128_offset(r, hi ? c1 + 2 : c1);
+      const uint32_t oB = hi * kBlkBytes + sw128_offset(r, hi ? c1 : c1 + 2);
+#pragma unroll
+      for (int m = 0; m < 2; ++m) {
+        if (m == 1 && tb == nullptr) break;
+        uint8_t* t = m ? tb : ta;
+        const uint4 vA = m ? xb[k][0] : xa[k][0], vB = m ? xb[k][1] : xa[k][1];
+        const uint32_t xA[4] = {vA.x, vA.y, vA.z, vA.w};
+        const uint32_t xB[4] = {vB.x, vB.y, vB.z, vB.w};
+        uint32_t yA[4], yB[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint64_t a2 = f2_pack(bf16_lo(xA[q]), bf16_hi(xA[q]));
+          const uint64_t b2 = f2_pack(bf16_lo(xB[q]), bf16_hi(xB[q]));
+          float y0, y1, z0, z1;
+          f2_unpack(fadd2(fmul2(a2, c2[q]), fmul2(b2, s2[q])), y0, y1);
+          f2_unpack(fsub2(fmul2(b2, c2[q]), fmul2(a2, s2[q])), z0, z1);
+          yA[q] = pack_bf16(y0, y1);
+          yB[q] = pack_bf16(z0, z1);
+        }
+        *reinterpret_cast<uint4*>(t + oA) = make_uint4(yA[0], yA[1], yA[2], yA[3]);
+        *reinterpret_cast<uint4*>(t + oB) = make_uint4(yB[0], yB[1], yB[2], yB[3]);
+      }
     }
   }
 }
@@ -389,8 +417,12 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
       if (!stop && own_k) stop = !mbar_wait(&bars[B_KFULL + 2 * t], 0);
       stop = __any_sync(0xffffffffu, stop);
       if (!stop) {
-        rope_rotate_tile<8>(qt, p.rope_cs, q_row0, p.S, row_in_tile, 128);
-        if (own_k) rope_rotate_tile<8>(kt, p.rope_cs, k_row0, p.kv_len, row_in_tile, 128);
+        if (own_k && k_row0 == q_row0) {  // (kv_len == S: the same tokens and limit)
+          rope_rotate_rows<4>(qt, kt, p.rope_cs, q_row0, p.S, row_in_tile, 128);
+        } else {
+          rope_rotate_rows<8>(qt, nullptr, p.rope_cs, q_row0, p.S, row_in_tile, 128);
+          if (own_k) rope_rotate_rows<8>(kt, nullptr, p.rope_cs, k_row0, p.kv_len, row_in_tile, 128);
+        }
       }
       fence_proxy_async_smem();
       if (named_bar_any(bar_id, 128, stop)) {
@@ -599,7 +631,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
         if (!(ok = mbar_wait_w(&bars[B_KFULL + s], (n / 10) & 1))) break;
         if (j < 2) continue;
         if (rot_mark[s]) {
-          rope_rotate_tile<8>(smem + kOffKV + s * kTileBytes, p.rope_cs,
+          rope_rotate_rows<8>(smem + kOffKV + s * kTileBytes, nullptr, p.rope_cs,
                               kv_tile_of(j, pair, nkv) * kKeys, p.kv_len, tid, 64);
           fence_proxy_async_smem();
         }

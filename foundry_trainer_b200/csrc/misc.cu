@@ -134,7 +134,12 @@ __global__ void rope_table2_kernel(const __grid_constant__ RopeArgs r, int S, fl
   const float2 cs = rope_cs_direct(r, t, f);
   const int64_t o = (int64_t)(t + r.pos_offset) * nf + f;
   table[o] = cs;
-  packed[o] = (__float_as_uint(cs.x) >> 16) | (__float_as_uint(cs.y) & 0xFFFF0000u);
+  // the packed row of a token with 64 frequencies is ordered for the forward
+  // kernel's quarter-warp reads: words 4i..4i+3 hold frequencies 8i..8i+3,
+  // words 32+4i..32+4i+3 hold 8i+4..8i+7
+  const int fp = nf == 64 ? ((f >> 2) & 1) * 32 + (f >> 3) * 4 + (f & 3) : f;
+  packed[o - f + fp] =
+      (__float_as_uint(cs.x) >> 16) | (__float_as_uint(cs.y) & 0xFFFF0000u);
 }
 
 // ------------------------------------------------ token-major fast paths

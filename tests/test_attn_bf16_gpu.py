@@ -235,6 +235,11 @@ def test_bf16_forward_in_tile_rotation_matches_rope_apply(B, S, H):
     k_rot = ws[tb:tb + n * 2].view(torch.bfloat16).view(shape)
     assert torch.equal(q_rot, ops.rope_apply(q, rope))
     assert torch.equal(k_rot, ops.rope_apply(k, rope))
+    # every K tile a CTA used, whether loaded rotated or rotated in its ring
+    # slot, held the same bits: O equals the forward on pre-rotated inputs
+    o_plain, lse_plain = ops.attn_fwd(ops.rope_apply(q, rope), ops.rope_apply(k, rope), v)
+    torch.cuda.synchronize()
+    assert torch.equal(o, o_plain) and torch.equal(lse, lse_plain)
     d_o = torch.zeros_like(q)
     ro, rlse, _, _, _ = orc.attn_fwd_bwd_bshd(np32(q), np32(k), np32(v), np32(d_o), "f32",
                                               rope_pos=pos.numpy())
