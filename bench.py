@@ -582,15 +582,34 @@ def main():
             torch.cuda.synchronize()
         if ops.device_status() != 0:
             raise RuntimeError("device-side bounded wait expired")
-        t0 = trace[0][1]
-        rows = [(name, t0.elapsed_time(e)) for name, e in trace]
-        allrows = [rows]
-        if world > 1:
-            allrows = [None] * world
-            dist.all_gather_object(allrows, rows)
-        if rank == 0:
-            for r, rr in enumerate(allrows):
-                print(f"rank {r}: " + " ".join(f"{nm}={t:.3f}" for nm, t in rr), flush=True)
+        def report(kind):
+            t0 = trace[0][1]
+            rows = [(name, t0.elapsed_time(e)) for name, e in trace]
+            allrows = [rows]
+            if world > 1:
+                allrows = [None] * world
+                dist.all_gather_object(allrows, rows)
+            if rank == 0:
+                for r, rr in enumerate(allrows):
+                    print(f"{kind} rank {r}: " + " ".join(f"{nm}={t:.3f}" for nm, t in rr),
+                          flush=True)
+        report("eager")
+        # the same schedule captured in a CUDA graph, as the timed step runs it
+        # (the events become record nodes; the last replay's times are read)
+        trace.clear()
+        g_tl = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_tl):
+            step(trace)
+        for _ in range(4):
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
+            g_tl.replay()
+            torch.cuda.synchronize()
+        if ops.device_status() != 0:
+            raise RuntimeError("device-side bounded wait expired")
+        report("graph")
+        del g_tl
         ex.close()
         if world > 1:
             dist.destroy_process_group()

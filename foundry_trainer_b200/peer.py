@@ -292,9 +292,10 @@ def _capturing() -> bool:
 
 
 def _mark(trace: Optional[list], name: str, stream=None) -> None:
-    """Appends (name, timing event recorded on `stream`) when tracing."""
+    """Appends (name, timing event recorded on `stream`) when tracing (inside
+    a CUDA-graph capture the event becomes a record node of the graph)."""
     if trace is not None:
-        e = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True, external=_capturing())
         e.record(stream if stream is not None else torch.cuda.current_stream())
         trace.append((name, e))
 
