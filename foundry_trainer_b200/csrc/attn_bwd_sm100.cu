@@ -108,6 +108,10 @@ struct Params {
   // order, so repeated runs give the same bits. nullptr: reduce-adds.
   float* dq_part;
   RopeArgs rope;            // rope.pos == nullptr: no rotation
+  // acc 0: 1 = dK / dV leave through TMA tile stores (tm_dk, tm_dv), staged
+  // in the K and V tiles' shared memory (free once the last MMA completed);
+  // 0 = plain stores from registers (a layout the tensor maps cannot encode)
+  int tma_out;
 };
 
 // Q tile visited at step i by the CTA of K/V tile `kv_tile`.
@@ -172,24 +176,67 @@ __device__ __forceinline__ void store_rows32_f32(const Params& p, bool is_dk, in
         make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
   __syncwarp();
   const int cc = lane & 7;
+  // The warp's 32 rows are consecutive rows of one buffer unless a segment
+  // boundary falls among them: their addresses then follow from the first
+  // row's (the per-row segment division and parameter lookup measured 40% of
+  // the epilogue at the sequence-parallel shard shape). Warp-uniform branch.
+  const int last = min(key0 + 31, p.kv_len - 1);
+  if (key0 < p.kv_len && (p.acc != 3 || key0 / p.seg == last / p.seg)) {
+    float* row0 = f32_row(p, is_dk, b, key0, h) + col0;
+    const int64_t rstride = (int64_t)p.H * 128;
 #pragma unroll
-  for (int it = 0; it < 8; ++it) {
-    const int rr = it * 4 + (lane >> 3);
-    float4 x = slab[rr * 8 + (cc ^ (rr & 7))];
-    const int key = key0 + rr;
-    if (key < p.kv_len) {
-      float4* dst = reinterpret_cast<float4*>(f32_row(p, is_dk, b, key, h) + col0) + cc;
-      if (p.acc == 1) {
-        const float4 a = *dst;
-        x.x += a.x;
-        x.y += a.y;
-        x.z += a.z;
-        x.w += a.w;
+    for (int it = 0; it < 8; ++it) {
+      const int rr = it * 4 + (lane >> 3);
+      float4 x = slab[rr * 8 + (cc ^ (rr & 7))];
+      if (key0 + rr < p.kv_len) {
+        float4* dst = reinterpret_cast<float4*>(row0 + rr * rstride) + cc;
+        if (p.acc == 1) {
+          const float4 a = *dst;
+          x.x += a.x;
+          x.y += a.y;
+          x.z += a.z;
+          x.w += a.w;
+        }
+        *dst = x;
       }
-      *dst = x;
+    }
+  } else {
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int rr = it * 4 + (lane >> 3);
+      float4 x = slab[rr * 8 + (cc ^ (rr & 7))];
+      const int key = key0 + rr;
+      if (key < p.kv_len) {
+        float4* dst = reinterpret_cast<float4*>(f32_row(p, is_dk, b, key, h) + col0) + cc;
+        if (p.acc == 1) {
+          const float4 a = *dst;
+          x.x += a.x;
+          x.y += a.y;
+          x.z += a.z;
+          x.w += a.w;
+        }
+        *dst = x;
+      }
     }
   }
   __syncwarp();
+}
+
+// Stages columns [32a, 32a+32) of bf16 row `r` of a (128 x 128) tile in
+// shared memory in the SWIZZLE_128B layout of the TMA tile store (two 64-
+// column blocks; chunk c of row r at c ^ (r & 7): the 32 rows of a warp
+// cover all bank groups).
+__device__ __forceinline__ void stage_chunk32(uint8_t* tile, int r, int a, const float* v) {
+  uint8_t* blk = tile + (a >> 1) * kBlkBytes;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint4 o;
+    o.x = pack_bf16(v[8 * c + 0], v[8 * c + 1]);
+    o.y = pack_bf16(v[8 * c + 2], v[8 * c + 3]);
+    o.z = pack_bf16(v[8 * c + 4], v[8 * c + 5]);
+    o.w = pack_bf16(v[8 * c + 6], v[8 * c + 7]);
+    *reinterpret_cast<uint4*>(blk + sw128_offset(r, (a & 1) * 4 + c)) = o;
+  }
 }
 
 // Writes columns [col0, col0+32) of one bf16 dK/dV row held in registers.
@@ -242,7 +289,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                 const __grid_constant__ CUtensorMap tm_k,
                 const __grid_constant__ CUtensorMap tm_v,
-                const __grid_constant__ CUtensorMap tm_do, const __grid_constant__ Params p) {
+                const __grid_constant__ CUtensorMap tm_do,
+                const __grid_constant__ CUtensorMap tm_dk,
+                const __grid_constant__ CUtensorMap tm_dv, const __grid_constant__ Params p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc);
@@ -467,8 +516,11 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                        key < p.kv_len;
     float4 cs[8], cs_next[8];
     if (unrot) load_axis_cs(p.rope, key, 0, cs);
-    if (ok && __all_sync(0xffffffffu, mbar_wait(&bars[B_FINAL], 0)) &&
-        !__any_sync(0xffffffffu, *abort_flag != 0)) {
+    const bool tma_out = p.acc == 0 && p.tma_out;
+    uint8_t* out_tile = smem + (is_dk ? kOffK : kOffV);
+    const bool good = ok && __all_sync(0xffffffffu, mbar_wait(&bars[B_FINAL], 0)) &&
+                      !__any_sync(0xffffffffu, *abort_flag != 0);
+    if (good) {
       tc_fence_after();
       const uint32_t t_acc = tmem + lane_off + (is_dk ? kColDK : kColDV);
 #pragma unroll
@@ -487,6 +539,8 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
           store_rows32_f32(p, is_dk, b, kv_tile * kRows + sub * 32, h, a * 32, v,
                            reinterpret_cast<float4*>(smem + kOffDS + (half * 4 + sub) * 4096),
                            lane);
+        else if (tma_out)
+          stage_chunk32(out_tile, key_in_tile, a, v);
         else if (key < p.kv_len)
           store_chunk32(p, is_dk, b, key, h, a * 32, v);
         if (unrot && a < 3) {
@@ -496,6 +550,18 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
       }
     } else {
       *abort_flag = 1;
+    }
+    if (tma_out) {
+      // the warpgroup's tile (rows past kv_len are clipped by the tensor map)
+      fence_proxy_async_smem();
+      const bool stop = half ? named_bar_any(4, 128, !good) : named_bar_any(3, 128, !good);
+      if (!stop && sub == 0 && lane == 0) {
+        const CUtensorMap* map = is_dk ? &tm_dk : &tm_dv;
+        tma_store_4d(map, out_tile, 0, kv_tile * kRows, h, b);
+        tma_store_4d(map, out_tile + kBlkBytes, 64, kv_tile * kRows, h, b);
+        bulk_commit_group();
+        bulk_wait_group_read0();  // shared memory read before the CTA exits
+      }
     }
   } else {
     // ------------------------------ dQ drain (head-dim column per thread)
@@ -614,7 +680,7 @@ int launch_attn_bwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
     return FA_ERR_UNSUPPORTED;  // the dK epilogue un-rotates 32-wide axes
   if (rope != nullptr && rope_table == nullptr)
     return FA_ERR_INVALID_ARG;  // ... with the (cos, sin) table
-  CUtensorMap tq, tk, tv, tdo;
+  CUtensorMap tq, tk, tv, tdo, tdk, tdv;
   int rc = make_tmap_bshd(&tq, q, sh.B, sh.S, sh.H, sh.D, 128);
   if (!rc) rc = make_tmap_bshd(&tk, k, sh.B, kv_len, sh.H, sh.D, 128);
   if (!rc) rc = make_tmap_bshd(&tv, v, sh.B, kv_len, sh.H, sh.D, 128);
@@ -655,12 +721,21 @@ int launch_attn_bwd_bf16(const AttnShape& sh, int kv_len, const fa_tensor_t* q,
   p.dq_part = dq_part;
   p.rope = make_rope_args(rope);
   p.rope.table = rope_table;
+  // bf16 dK / dV through TMA tile stores when both layouts encode (else the
+  // maps are copies of tk / tv and are never used)
+  p.tma_out = p.acc == 0 && dk != nullptr && dv != nullptr &&
+              make_tmap_bshd(&tdk, dk, sh.B, kv_len, sh.H, sh.D, 128) == FA_OK &&
+              make_tmap_bshd(&tdv, dv, sh.B, kv_len, sh.H, sh.D, 128) == FA_OK;
+  if (!p.tma_out) {
+    tdk = tk;
+    tdv = tv;
+  }
   rc = ensure_smem_attr((const void*)bwd::attn_bwd_kernel, bwd::kSmemBytes,
                         kKernelBwdBf16);
   if (rc) return rc;
   dim3 grid((kv_len + 127) / 128, sh.H, sh.B);
   bwd::attn_bwd_kernel<<<grid, bwd::kThreads, bwd::kSmemBytes, stream>>>(
-      tq, tk, tv, tdo, p);
+      tq, tk, tv, tdo, tdk, tdv, p);
   return launch_status();
 }
 

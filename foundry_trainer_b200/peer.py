@@ -347,9 +347,9 @@ def peer_fwd(q, k, v, pos, scale, ex: PeerExchange, kern: PeerKernels,
     for t in range(1, W):
         ex.pull(par, order[t], t, 0, k_all, cs)
         ex.pull(par, order[t], t, 1, v_all, cs)
+        _mark(trace, f"pull{t}", cs)  # (before `landed`, which the folds join)
         landed[t] = torch.cuda.Event()
         landed[t].record(cs)
-        _mark(trace, f"pull{t}", cs)
     # two fp32 (O, LSE) accumulators folded on two streams, then merged
     acc = [(torch.empty((B, S, H, D), device=dev, dtype=torch.float32),
             torch.empty((B, H, S), device=dev, dtype=torch.float32)) for _ in range(2)]
