@@ -16,7 +16,10 @@ the long-sequence case sequence-parallel instead: one sequence of 16896 rows
 sharded over the ranks (strong scaling); the K/V shards and the dK/dV
 contributions cross NVLink through peer memory (`--transport peer`, the
 default: copy-engine pulls, stores from the backward's epilogue, device
-barriers) or an NCCL send/recv ring (`--transport nccl`).
+barriers), or an NCCL send/recv ring (`--transport nccl`); or (`--transport
+heads`) two NCCL all-to-alls per pass turn the sequence shards into head
+groups, and each rank runs the single-GPU op on its H/N heads over the whole
+sequence (foundry_trainer_b200/heads.py).
 
 Rank 0 prints one JSON line: the metric (TFLOP/s, FlashAttention accounting
 14*B*H*S^2*D), the roofline of the dominant kernel (the backward kernel,
@@ -444,9 +447,10 @@ def main():
                          "configuration) and c5 on N > 1 (one 16896-row sequence "
                          "sharded over the ranks: the sequence-parallel NVLink path)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--transport", default="peer", choices=["peer", "nccl"],
-                    help="c5 exchange: peer memory (copy-engine pulls, peer stores, device "
-                         "barriers) or NCCL send/recv round a ring")
+    ap.add_argument("--transport", default="peer", choices=["heads", "peer", "nccl"],
+                    help="c5 exchange: head groups by NCCL all-to-all (heads), peer memory "
+                         "(copy-engine pulls, peer stores, device barriers) or NCCL send/recv "
+                         "round a ring")
     ap.add_argument("--peer-copy", default="ce", choices=["ce", "sm"],
                     help="peer transport: K/V pulled by the copy engines (ce) or by a copy "
                          "kernel beside the attention CTAs (sm)")
@@ -523,6 +527,20 @@ def main():
                     outs["dq"], outs["dk"], outs["dv"] = peer.peer_bwd(
                         q_r, k_all, v_all, o_, d_o, lse_, pos, scale, ex, pkern, trace,
                         check_status=False)
+                return step, outs
+        elif args.transport == "heads":
+            from foundry_trainer_b200 import heads as hpar
+            hex_, hkern = hpar.HeadExchange(), hpar.HeadKernels()
+            pos_all = pos_full.contiguous().to(dev)  # every rank attends the whole sequence
+
+            def make_step(q, k, v, d_o):
+                outs = {}
+
+                def step():
+                    o_, state = hpar.head_fwd(q, k, v, pos_all, scale, hex_, hkern)
+                    outs["o"] = o_
+                    outs["dq"], outs["dk"], outs["dv"] = hpar.head_bwd(d_o, state, scale, hex_,
+                                                                       hkern)
                 return step, outs
         else:
             comm, kern = ring.RingComm(), ring.RingKernels()
@@ -638,9 +656,10 @@ def main():
     # The timed step replays a CUDA graph of the same public-API calls, so
     # host-side launch overhead (ctypes, descriptor encoding) is not timed as
     # device idle; per-kernel times come from an eager pass with the event hooks.
-    # The NCCL ring step holds NCCL exchanges and runs eagerly; the peer
-    # step (copies, device barriers, kernels on three streams) is captured.
-    if ring_mode and args.transport == "nccl":
+    # The NCCL ring and head-group steps hold NCCL exchanges and run eagerly;
+    # the peer step (copies, device barriers, kernels on three streams) is
+    # captured.
+    if ring_mode and args.transport in ("nccl", "heads"):
         run = step
     else:
         graph = torch.cuda.CUDAGraph()
@@ -711,7 +730,8 @@ def main():
     peak_kind = "bf16_sustained" if timed_seconds > 2.0 else "bf16"
     peak = peaks[peak_kind]
     # the peer path's backward is one launch over all W shards' keys
-    bwd_flops = 2.5 * blk * (world if ring_mode and args.transport == "peer" else 1)
+    # (as is the head-group backward: all S rows, H / W heads)
+    bwd_flops = 2.5 * blk * (world if ring_mode and args.transport in ("peer", "heads") else 1)
     achieved = bwd_flops / (bwd_ms / 1e3) / 1e12
     traffic = None
     tf = ROOT / "profiles" / "traffic.json"
@@ -843,6 +863,9 @@ def main():
                "ms_per_step": te.item() / K,
                "path": ("ring.ring_fwd + ring.ring_bwd (C ABI fa_fwd_partial/fa_bwd_partial "
                         "round an NCCL ring)" if ring_mode and args.transport == "nccl" else
+                        "heads.head_fwd + heads.head_bwd (NCCL all-to-alls; C ABI fa_fwd/"
+                        "fa_bwd_saved on H/W heads)" if ring_mode and args.transport == "heads"
+                        else
                         "peer.peer_fwd + peer.peer_bwd (C ABI fa_fwd_fold/fa_merge_f32/"
                         "fa_bwd_scatter/fa_reduce_cast_f32 over peer memory)" if ring_mode else
                         "ops.attn_fwd + ops.attn_bwd (C ABI fa_fwd/fa_bwd_saved)") +
@@ -877,6 +900,16 @@ def main():
         parallelism = (f"sequence-parallel x{world} over peer memory (K/V pulled by "
                        f"{'a copy kernel' if args.peer_copy == 'sm' else 'the copy engines'}, "
                        f"dK/dV rows stored into the owners by the backward's epilogue)")
+    elif ring_mode and args.transport == "heads":
+        # fwd: table + fwd kernel; bwd: delta + bwd kernel + dQ finish (the
+        # all-to-alls are NCCL's kernels, not counted)
+        launches_per_step = 5
+        workload = (f"{cfg.name}: B={cfg.B} H={cfg.H} S={cfg.S} ({cfg.txt} text + "
+                    f"{cfg.grid}x{cfg.grid} image) D={cfg.D}, one sequence sharded "
+                    f"{n_loc} rows per rank, non-causal, axial RoPE inside the op")
+        parallelism = (f"head groups x{world}: NCCL all-to-all of q,k,v / O / dO / dq,dk,dv "
+                       f"between the sequence shards and {cfg.H // world} heads per rank over "
+                       f"the whole sequence")
     elif ring_mode:
         # fwd: rope q, rope k, W blocks + W merges, O cast; bwd: prepare,
         # W blocks, W-1 accumulator adds, 3 casts
