@@ -45,7 +45,8 @@ class HeadExchange:
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
 
     def all_to_all(self, recv: torch.Tensor, send: torch.Tensor) -> None:
-        """recv[i] <- rank i's send[self.rank] (equal splits of dim 0)."""
+        """recv[i] <- rank i's send[self.rank] (equal splits of dim 0; both
+        contiguous)."""
         if self.world == 1:
             recv.copy_(send)
         else:
@@ -54,40 +55,46 @@ class HeadExchange:
 
 def seq_to_heads(xs: Sequence[torch.Tensor], ex: HeadExchange) -> List[torch.Tensor]:
     """(B, S_loc, H, D) sequence shards -> (B, W*S_loc, H/W, D): this rank's
-    head group over the whole sequence, one exchange for all of `xs`."""
+    head group over the whole sequence. One exchange per tensor: the send
+    side regroups the shard by destination (one copy); with B = 1 the
+    received blocks already are the head group's rows in order, so they land
+    in the result without a second copy."""
     W = ex.world
-    B, S_loc, H, D = xs[0].shape
-    if H % W:
-        raise ValueError(f"{H} heads do not split over {W} ranks")
-    hw, n = H // W, len(xs)
-    send = torch.empty((W, n, B, S_loc, hw, D), device=xs[0].device, dtype=xs[0].dtype)
-    for j, x in enumerate(xs):
-        send[:, j].copy_(x.reshape(B, S_loc, W, hw, D).permute(2, 0, 1, 3, 4))
-    recv = torch.empty_like(send)
-    ex.all_to_all(recv, send)
     outs = []
-    for j in range(n):
-        y = torch.empty((B, W * S_loc, hw, D), device=recv.device, dtype=recv.dtype)
-        y.view(B, W, S_loc, hw, D).copy_(recv[:, j].permute(1, 0, 2, 3, 4))
+    for x in xs:
+        B, S_loc, H, D = x.shape
+        if H % W:
+            raise ValueError(f"{H} heads do not split over {W} ranks")
+        hw = H // W
+        send = x.reshape(B, S_loc, W, hw, D).permute(2, 0, 1, 3, 4).contiguous()
+        y = torch.empty((B, W * S_loc, hw, D), device=x.device, dtype=x.dtype)
+        if B == 1:
+            ex.all_to_all(y.view(W, B, S_loc, hw, D), send)
+        else:
+            recv = torch.empty_like(send)
+            ex.all_to_all(recv, send)
+            y.view(B, W, S_loc, hw, D).copy_(recv.permute(1, 0, 2, 3, 4))
         outs.append(y)
     return outs
 
 
 def heads_to_seq(xs: Sequence[torch.Tensor], ex: HeadExchange) -> List[torch.Tensor]:
     """Inverse of seq_to_heads: (B, W*S_loc, H/W, D) head groups ->
-    (B, S_loc, H, D) this rank's sequence shard of all heads."""
+    (B, S_loc, H, D) this rank's sequence shard of all heads (with B = 1 the
+    send blocks are contiguous row ranges: one copy, on the receive side)."""
     W = ex.world
-    B, S, hw, D = xs[0].shape
-    S_loc, n = S // W, len(xs)
-    send = torch.empty((W, n, B, S_loc, hw, D), device=xs[0].device, dtype=xs[0].dtype)
-    for j, x in enumerate(xs):
-        send[:, j].copy_(x.reshape(B, W, S_loc, hw, D).permute(1, 0, 2, 3, 4))
-    recv = torch.empty_like(send)
-    ex.all_to_all(recv, send)
     outs = []
-    for j in range(n):
-        y = torch.empty((B, S_loc, W * hw, D), device=recv.device, dtype=recv.dtype)
-        y.view(B, S_loc, W, hw, D).copy_(recv[:, j].permute(1, 2, 0, 3, 4))
+    for x in xs:
+        B, S, hw, D = x.shape
+        S_loc = S // W
+        if B == 1:
+            send = x.reshape(W, B, S_loc, hw, D)
+        else:
+            send = x.reshape(B, W, S_loc, hw, D).permute(1, 0, 2, 3, 4).contiguous()
+        recv = torch.empty((W, B, S_loc, hw, D), device=x.device, dtype=x.dtype)
+        ex.all_to_all(recv, send)
+        y = torch.empty((B, S_loc, W * hw, D), device=x.device, dtype=x.dtype)
+        y.view(B, S_loc, W, hw, D).copy_(recv.permute(1, 2, 0, 3, 4))
         outs.append(y)
     return outs
 
